@@ -1,0 +1,174 @@
+/*
+ * attnres_b200.h — C ABI of the B200 (sm_100a) block Attention-Residual
+ * depth-routing read ("AttnRes" / low-rank "LRID" read), forward and backward.
+ *
+ * The ABI takes plain device pointers, element strides and sizes; it never
+ * allocates device memory and never synchronises the host. Every call enqueues
+ * its kernels on the caller's CUDA stream (`stream` is a cudaStream_t; NULL is
+ * the legacy default stream).
+ *
+ * Geometry used throughout:
+ *   S  = num_sources   depth sources read by one residual site (1..ATTNRES_MAX_SOURCES)
+ *   N  = num_tokens    token rows (B*T); row n of source s starts at base_s + n*row_stride_s
+ *   d  = value_dim     value width, split into H heads of dv = d/H columns
+ *   R  = key_dim       low-rank key width, split into H heads of dk = R/H columns
+ *   H  = num_heads     depth heads
+ *
+ * All value/key/query/output tensors of one call share one element type
+ * (`dtype`, an attnres_dtype). The last dimension of every source is dense
+ * (element stride 1); rows may be strided (e.g. keys that are a column slice of
+ * a wider projection). Outputs are dense row-major.
+ *
+ * Status codes: 0 on success, otherwise an attnres_status; a message for the
+ * last failure on the calling host thread is returned by attnres_last_error().
+ *
+ * Reference interfaces replaced (paths inside jon123boss/LR-AttnRes):
+ *   attnres_lrid_forward   <- torch.library op attnres::lrid_read_list
+ *                             (attnres_ops.py:4636-4722) and the Triton kernel
+ *                             _lrid_attnres_list_read_kernel (attnres_ops.py:331-445),
+ *                             plus _lrid_read_list_triton (attnres_ops.py:4533-4629)
+ *   attnres_lrid_backward  <- attnres::lrid_read_list_backward (attnres_ops.py:4725-4802),
+ *                             _lrid_attnres_list_backward_kernel (attnres_ops.py:602-746)
+ *                             and _lrid_read_list_backward_triton (attnres_ops.py:4373-4456)
+ *   attnres_base_forward   <- _attnres_read_list_triton / _attnres_list_read_kernel
+ *                             (attnres_ops.py:2301-2342, :267-328)
+ *   attnres_base_backward  <- _attnres_read_list_backward_triton /
+ *                             _attnres_list_backward_kernel (attnres_ops.py:2378-2421, :448-535)
+ */
+#ifndef ATTNRES_B200_H
+#define ATTNRES_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ATTNRES_ABI_VERSION 1
+#define ATTNRES_MAX_SOURCES 64
+
+typedef enum attnres_dtype {
+  ATTNRES_DTYPE_F32 = 0,
+  ATTNRES_DTYPE_F16 = 1,
+  ATTNRES_DTYPE_BF16 = 2
+} attnres_dtype;
+
+typedef enum attnres_status {
+  ATTNRES_OK = 0,
+  ATTNRES_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad enum */
+  ATTNRES_ERR_UNSUPPORTED = 2,      /* shape/alignment outside what the kernels handle */
+  ATTNRES_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
+  ATTNRES_ERR_WORKSPACE = 4         /* workspace missing or smaller than required */
+} attnres_status;
+
+/* How the depth query is formed (model.py:2102-2115 of the reference). */
+typedef enum attnres_query_mode {
+  ATTNRES_QUERY_STATIC = 0,  /* query [H, dk], shared by all tokens                     */
+  ATTNRES_QUERY_DYNAMIC = 1, /* query_dynamic [N, H, dk], one query per token           */
+  ATTNRES_QUERY_GATED = 2    /* q_t = query[H,dk] + gate[H] * query_dynamic[N,H,dk]      */
+} attnres_query_mode;
+
+/* RMS normalisation of the read output. */
+typedef enum attnres_norm_mode {
+  ATTNRES_NORM_NONE = 0,
+  ATTNRES_NORM_PER_HEAD = 1, /* rms over each head's dv columns; inv-rms saved as [N, H] */
+  ATTNRES_NORM_ROW = 2       /* rms over all d columns;          inv-rms saved as [N]    */
+} attnres_norm_mode;
+
+int attnres_abi_version(void);
+const char* attnres_last_error(void);
+
+/*
+ * LRID read, forward. Replaces attnres::lrid_read_list (attnres_ops.py:4636).
+ *   logit[n,h,s] = logit_scale * <khat[s,n,h,:], q[n,h,:]> + logit_bias[s]
+ *   khat         = key_norm ? k * rsqrt(mean(k^2) + key_eps) : k     (per head of dk)
+ *   alpha        = softmax over s (fp32)
+ *   out[n,h,:]   = sum_s alpha[n,h,s] * V[s,n,h,:]   (fp32 accumulate, rounded to dtype)
+ * query / query_gate / query_dynamic are dtype; unused ones may be NULL.
+ * logit_bias: float[S] or NULL. output_inv_rms: float[N,H] (PER_HEAD) or float[N]
+ * (ROW) or NULL. alpha_out / key_inv_rms_out: float[N,H,S] or NULL.
+ */
+int attnres_lrid_forward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                         int num_heads, int dtype,
+                         const void* const* values, const int64_t* value_row_strides,
+                         const void* const* keys, const int64_t* key_row_strides,
+                         int query_mode, const void* query, const void* query_gate,
+                         const void* query_dynamic, float logit_scale, int key_norm,
+                         float key_eps, const float* logit_bias, int output_norm,
+                         float output_eps, void* output, float* output_inv_rms,
+                         float* alpha_out, float* key_inv_rms_out, void* stream);
+
+/*
+ * Bytes of device workspace attnres_lrid_backward needs for this geometry on
+ * the current device (deterministic per-CTA partial sums of the parameter
+ * gradients). Returns 0 when the geometry is invalid.
+ */
+size_t attnres_lrid_backward_workspace_bytes(int num_sources, int64_t num_tokens,
+                                             int value_dim, int key_dim, int num_heads,
+                                             int dtype);
+
+/*
+ * LRID read, backward. Replaces attnres::lrid_read_list_backward (attnres_ops.py:4725).
+ * Softmax weights are recomputed from the keys (same arithmetic as the forward).
+ *   grad_values[s] : dtype [N, d] dense  = alpha * g'            (g' = output-norm backward of g)
+ *   grad_keys[s]   : dtype [N, R] dense  = key-norm backward of dlogit*scale*q
+ *   grad_query     : STATIC/GATED: float [H, dk] summed over tokens (deterministic order)
+ *                    DYNAMIC     : dtype [N, H, dk] per token
+ *   grad_query_gate    : GATED only, float [H]
+ *   grad_query_dynamic : GATED only, dtype [N, H, dk] (= gate * per-token dq)
+ *   grad_logit_bias    : float [S] or NULL
+ * normed_output / output_inv_rms: the forward's normalised output and inv-rms,
+ * required when output_norm != NONE.
+ * The per-token gradients are written once; the summed ones are reduced in a
+ * fixed order, so repeated calls are bitwise identical.
+ */
+int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                          int num_heads, int dtype,
+                          const void* const* values, const int64_t* value_row_strides,
+                          const void* const* keys, const int64_t* key_row_strides,
+                          int query_mode, const void* query, const void* query_gate,
+                          const void* query_dynamic, float logit_scale, int key_norm,
+                          float key_eps, const float* logit_bias, int output_norm,
+                          float output_eps, const void* grad_output, const void* normed_output,
+                          const float* output_inv_rms, void* const* grad_values,
+                          void* const* grad_keys, void* grad_query, float* grad_query_gate,
+                          void* grad_query_dynamic, float* grad_logit_bias, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/*
+ * Base AttnRes read, forward (keys are the values themselves).
+ * Replaces _attnres_read_list_triton (attnres_ops.py:2301) /
+ * _attnres_list_read_kernel (attnres_ops.py:267).
+ *   khat = key_norm ? v * rsqrt(mean(v^2) + key_eps) : v ;  logit = <khat, query> + bias
+ * query: dtype [d]. output_norm: NONE or ROW; output_inv_rms float[N] or NULL.
+ */
+int attnres_base_forward(int num_sources, int64_t num_tokens, int value_dim, int dtype,
+                         const void* const* values, const int64_t* value_row_strides,
+                         const void* query, int key_norm, float key_eps,
+                         const float* logit_bias, int output_norm, float output_eps,
+                         void* output, float* output_inv_rms, void* stream);
+
+size_t attnres_base_backward_workspace_bytes(int num_sources, int64_t num_tokens,
+                                             int value_dim, int dtype);
+
+/*
+ * Base AttnRes read, backward. Replaces _attnres_read_list_backward_triton
+ * (attnres_ops.py:2378) / _attnres_list_backward_kernel (attnres_ops.py:448).
+ *   grad_values[s] : dtype [N, d] dense = alpha*g' + key-norm backward of dlogit*q
+ *   grad_query     : float [d] summed over tokens in a fixed order
+ */
+int attnres_base_backward(int num_sources, int64_t num_tokens, int value_dim, int dtype,
+                          const void* const* values, const int64_t* value_row_strides,
+                          const void* query, int key_norm, float key_eps,
+                          const float* logit_bias, int output_norm, float output_eps,
+                          const void* grad_output, const void* normed_output,
+                          const float* output_inv_rms, void* const* grad_values,
+                          float* grad_query, float* grad_logit_bias, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTNRES_B200_H */

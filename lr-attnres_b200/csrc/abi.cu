@@ -1,0 +1,337 @@
+// extern "C" entry points of libattnres_b200.so: argument validation, launch
+// planning, and error reporting. Declared in include/attnres_b200.h.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "common.cuh"
+#include "plan.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(ATTNRES_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int elem_size(int dtype) {
+  switch (dtype) {
+    case ATTNRES_DTYPE_F32: return 4;
+    case ATTNRES_DTYPE_F16:
+    case ATTNRES_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Common checks of the source tables. `need_keys` is false for the base read.
+int check_sources(int S, long long N, int d, int R, int H, int dtype, const void* const* values,
+                  const int64_t* vstr, const void* const* keys, const int64_t* kstr,
+                  bool need_keys) {
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (S < 1 || S > ATTNRES_MAX_SOURCES)
+    return fail(ATTNRES_ERR_UNSUPPORTED, "num_sources=%d outside [1, %d]", S, ATTNRES_MAX_SOURCES);
+  if (N < 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "num_tokens=%lld is negative", N);
+  if (d < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "value_dim=%d must be positive", d);
+  if (!values || !vstr) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "values/value_row_strides is NULL");
+  if (need_keys) {
+    if (H < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "num_heads=%d must be positive", H);
+    if (R < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "key_dim=%d must be positive", R);
+    if (d % H || R % H)
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "value_dim=%d and key_dim=%d must divide by num_heads=%d",
+                  d, R, H);
+    if (!keys || !kstr) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "keys/key_row_strides is NULL");
+  }
+  for (int s = 0; s < S; ++s) {
+    if (N > 0 && !values[s]) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "values[%d] is NULL", s);
+    if (vstr[s] < d) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "value_row_strides[%d]=%lld < value_dim",
+                                 s, (long long)vstr[s]);
+    if (need_keys) {
+      if (N > 0 && !keys[s]) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "keys[%d] is NULL", s);
+      if (kstr[s] < R) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "key_row_strides[%d]=%lld < key_dim",
+                                   s, (long long)kstr[s]);
+    }
+  }
+  return ATTNRES_OK;
+}
+
+// True when every value row (and the extra dense buffers) admits 16-byte packs.
+bool values_vectorizable(int S, int esz, const void* const* values, const int64_t* vstr,
+                         const void* const* extra, int n_extra) {
+  for (int s = 0; s < S; ++s)
+    if (!aligned16(values[s]) || (vstr[s] * esz) % 16) return false;
+  for (int i = 0; i < n_extra; ++i)
+    if (extra[i] && !aligned16(extra[i])) return false;
+  return true;
+}
+
+int check_query(int qmode, const void* q, const void* gate, const void* qdyn) {
+  switch (qmode) {
+    case ATTNRES_QUERY_STATIC:
+      if (!q) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "static query is NULL");
+      return ATTNRES_OK;
+    case ATTNRES_QUERY_DYNAMIC:
+      if (!qdyn) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "query_dynamic is NULL");
+      return ATTNRES_OK;
+    case ATTNRES_QUERY_GATED:
+      if (!q || !gate || !qdyn)
+        return fail(ATTNRES_ERR_INVALID_ARGUMENT, "gated query needs query, query_gate and query_dynamic");
+      return ATTNRES_OK;
+    default:
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown query_mode %d", qmode);
+  }
+}
+
+int check_norm(int mode, bool allow_per_head) {
+  if (mode == ATTNRES_NORM_NONE || mode == ATTNRES_NORM_ROW) return ATTNRES_OK;
+  if (mode == ATTNRES_NORM_PER_HEAD && allow_per_head) return ATTNRES_OK;
+  return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unsupported output_norm mode %d", mode);
+}
+
+}  // namespace
+
+extern "C" {
+
+int attnres_abi_version(void) { return ATTNRES_ABI_VERSION; }
+
+const char* attnres_last_error(void) { return g_last_error.c_str(); }
+
+int attnres_lrid_forward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                         int num_heads, int dtype, const void* const* values,
+                         const int64_t* value_row_strides, const void* const* keys,
+                         const int64_t* key_row_strides, int query_mode, const void* query,
+                         const void* query_gate, const void* query_dynamic, float logit_scale,
+                         int key_norm, float key_eps, const float* logit_bias, int output_norm,
+                         float output_eps, void* output, float* output_inv_rms, float* alpha_out,
+                         float* key_inv_rms_out, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values,
+                         value_row_strides, keys, key_row_strides, true);
+  if (rc) return rc;
+  if ((rc = check_query(query_mode, query, query_gate, query_dynamic))) return rc;
+  if ((rc = check_norm(output_norm, true))) return rc;
+  if (num_tokens > 0 && !output) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "output is NULL");
+  const int esz = elem_size(dtype);
+  const void* extra[1] = {output};
+  const bool vec = values_vectorizable(num_sources, esz, values, value_row_strides, extra, 1);
+  attnres::LridPlan plan;
+  const char* why = "";
+  rc = attnres::make_lrid_plan(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, vec,
+                               output_norm, &plan, &why);
+  if (rc) return fail(rc, "%s", why);
+  if (num_tokens == 0) return ATTNRES_OK;
+  attnres::LridIO io{values, value_row_strides, keys, key_row_strides, query_mode, query,
+                     query_gate, query_dynamic, logit_scale, key_norm, key_eps, logit_bias,
+                     output_norm, output_eps, output, output_inv_rms, alpha_out, key_inv_rms_out};
+  cudaError_t e = attnres::lrid_forward_launch(dtype, plan, io, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_forward launch");
+  return ATTNRES_OK;
+}
+
+size_t attnres_lrid_backward_workspace_bytes(int num_sources, int64_t num_tokens, int value_dim,
+                                             int key_dim, int num_heads, int dtype) {
+  if (elem_size(dtype) == 0 || num_sources < 1 || num_sources > ATTNRES_MAX_SOURCES ||
+      num_tokens < 0 || num_heads < 1 || value_dim < 1 || key_dim < 1 ||
+      value_dim % num_heads || key_dim % num_heads)
+    return 0;
+  attnres::LridPlan plan;
+  const char* why = "";
+  // The pack width (and with it the grid) depends on pointer alignment, which
+  // is unknown here: size for the larger of the two launch shapes.
+  size_t best = 0;
+  for (int v = 0; v < 2; ++v) {
+    if (attnres::make_lrid_plan(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype,
+                                v == 1, ATTNRES_NORM_NONE, &plan, &why))
+      continue;
+    size_t b = 0;
+    if (attnres::lrid_workspace(dtype, plan, &b) != cudaSuccess) return 0;
+    if (b > best) best = b;
+  }
+  return best;
+}
+
+int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                          int num_heads, int dtype, const void* const* values,
+                          const int64_t* value_row_strides, const void* const* keys,
+                          const int64_t* key_row_strides, int query_mode, const void* query,
+                          const void* query_gate, const void* query_dynamic, float logit_scale,
+                          int key_norm, float key_eps, const float* logit_bias, int output_norm,
+                          float output_eps, const void* grad_output, const void* normed_output,
+                          const float* output_inv_rms, void* const* grad_values,
+                          void* const* grad_keys, void* grad_query, float* grad_query_gate,
+                          void* grad_query_dynamic, float* grad_logit_bias, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values,
+                         value_row_strides, keys, key_row_strides, true);
+  if (rc) return rc;
+  if ((rc = check_query(query_mode, query, query_gate, query_dynamic))) return rc;
+  if ((rc = check_norm(output_norm, true))) return rc;
+  if (!grad_values || !grad_keys)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_values/grad_keys is NULL");
+  if (num_tokens > 0) {
+    if (!grad_output) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_output is NULL");
+    if (output_norm != ATTNRES_NORM_NONE && (!normed_output || !output_inv_rms))
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "output norm backward needs normed_output and output_inv_rms");
+    for (int s = 0; s < num_sources; ++s)
+      if (!grad_values[s] || !grad_keys[s])
+        return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_values[%d]/grad_keys[%d] is NULL", s, s);
+  }
+  if (!grad_query) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_query is NULL");
+  if (query_mode == ATTNRES_QUERY_GATED && (!grad_query_gate || (num_tokens > 0 && !grad_query_dynamic)))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "gated query needs grad_query_gate and grad_query_dynamic");
+  const int esz = elem_size(dtype);
+  const void* extra[2 + ATTNRES_MAX_SOURCES];
+  int n_extra = 0;
+  extra[n_extra++] = grad_output;
+  extra[n_extra++] = output_norm != ATTNRES_NORM_NONE ? normed_output : nullptr;
+  for (int s = 0; s < num_sources; ++s) extra[n_extra++] = grad_values[s];
+  const bool vec = values_vectorizable(num_sources, esz, values, value_row_strides, extra, n_extra);
+  attnres::LridPlan plan;
+  const char* why = "";
+  rc = attnres::make_lrid_plan(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, vec,
+                               output_norm, &plan, &why);
+  if (rc) return fail(rc, "%s", why);
+  const bool need_ws = query_mode != ATTNRES_QUERY_DYNAMIC || grad_logit_bias != nullptr;
+  if (need_ws) {
+    size_t need = 0;
+    cudaError_t e = attnres::lrid_workspace(dtype, plan, &need);
+    if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward workspace query");
+    if (!workspace || workspace_bytes < need)
+      return fail(ATTNRES_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+    if (!aligned16(workspace)) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  }
+  attnres::LridIO io{values, value_row_strides, keys, key_row_strides, query_mode, query,
+                     query_gate, query_dynamic, logit_scale, key_norm, key_eps, logit_bias,
+                     output_norm, output_eps, nullptr, nullptr, nullptr, nullptr};
+  attnres::LridGradIO gio{grad_output, normed_output, output_inv_rms, grad_values, grad_keys,
+                          grad_query, grad_query_gate, grad_query_dynamic, grad_logit_bias, workspace};
+  cudaError_t e = attnres::lrid_backward_launch(dtype, plan, io, gio, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward launch");
+  return ATTNRES_OK;
+}
+
+int attnres_base_forward(int num_sources, int64_t num_tokens, int value_dim, int dtype,
+                         const void* const* values, const int64_t* value_row_strides,
+                         const void* query, int key_norm, float key_eps, const float* logit_bias,
+                         int output_norm, float output_eps, void* output, float* output_inv_rms,
+                         void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, 0, 1, dtype, values,
+                         value_row_strides, nullptr, nullptr, false);
+  if (rc) return rc;
+  if ((rc = check_norm(output_norm, false))) return rc;
+  if (!query) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "query is NULL");
+  if (num_tokens > 0 && !output) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "output is NULL");
+  const void* extra[2] = {output, query};
+  const bool vec = values_vectorizable(num_sources, elem_size(dtype), values, value_row_strides, extra, 2);
+  attnres::BasePlan plan;
+  const char* why = "";
+  rc = attnres::make_base_plan(num_sources, num_tokens, value_dim, dtype, vec, &plan, &why);
+  if (rc) return fail(rc, "%s", why);
+  if (num_tokens == 0) return ATTNRES_OK;
+  attnres::BaseIO io{};
+  io.values = values;
+  io.vstr = value_row_strides;
+  io.q = query;
+  io.key_norm = key_norm;
+  io.key_eps = key_eps;
+  io.bias = logit_bias;
+  io.out_norm = output_norm;
+  io.out_eps = output_eps;
+  io.out = output;
+  io.out_inv = output_inv_rms;
+  cudaError_t e = attnres::base_forward_launch(dtype, plan, io, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_base_forward launch");
+  return ATTNRES_OK;
+}
+
+size_t attnres_base_backward_workspace_bytes(int num_sources, int64_t num_tokens, int value_dim,
+                                             int dtype) {
+  if (elem_size(dtype) == 0 || num_sources < 1 || num_sources > ATTNRES_MAX_SOURCES ||
+      num_tokens < 0 || value_dim < 1)
+    return 0;
+  size_t best = 0;
+  for (int v = 0; v < 2; ++v) {
+    attnres::BasePlan plan;
+    const char* why = "";
+    if (attnres::make_base_plan(num_sources, num_tokens, value_dim, dtype, v == 1, &plan, &why))
+      continue;
+    size_t b = 0;
+    if (attnres::base_workspace(dtype, plan, &b) != cudaSuccess) return 0;
+    if (b > best) best = b;
+  }
+  return best;
+}
+
+int attnres_base_backward(int num_sources, int64_t num_tokens, int value_dim, int dtype,
+                          const void* const* values, const int64_t* value_row_strides,
+                          const void* query, int key_norm, float key_eps, const float* logit_bias,
+                          int output_norm, float output_eps, const void* grad_output,
+                          const void* normed_output, const float* output_inv_rms,
+                          void* const* grad_values, float* grad_query, float* grad_logit_bias,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, 0, 1, dtype, values,
+                         value_row_strides, nullptr, nullptr, false);
+  if (rc) return rc;
+  if ((rc = check_norm(output_norm, false))) return rc;
+  if (!query || !grad_query) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "query/grad_query is NULL");
+  if (!grad_values) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_values is NULL");
+  if (num_tokens > 0) {
+    if (!grad_output) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_output is NULL");
+    if (output_norm != ATTNRES_NORM_NONE && (!normed_output || !output_inv_rms))
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "output norm backward needs normed_output and output_inv_rms");
+    for (int s = 0; s < num_sources; ++s)
+      if (!grad_values[s]) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_values[%d] is NULL", s);
+  }
+  const void* extra[3 + ATTNRES_MAX_SOURCES];
+  int n_extra = 0;
+  extra[n_extra++] = grad_output;
+  extra[n_extra++] = query;
+  extra[n_extra++] = output_norm != ATTNRES_NORM_NONE ? normed_output : nullptr;
+  for (int s = 0; s < num_sources; ++s) extra[n_extra++] = grad_values[s];
+  const bool vec = values_vectorizable(num_sources, elem_size(dtype), values, value_row_strides, extra, n_extra);
+  attnres::BasePlan plan;
+  const char* why = "";
+  rc = attnres::make_base_plan(num_sources, num_tokens, value_dim, dtype, vec, &plan, &why);
+  if (rc) return fail(rc, "%s", why);
+  size_t need = 0;
+  cudaError_t e = attnres::base_workspace(dtype, plan, &need);
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_base_backward workspace query");
+  if (!workspace || workspace_bytes < need)
+    return fail(ATTNRES_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+  if (!aligned16(workspace)) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  attnres::BaseIO io{};
+  io.values = values;
+  io.vstr = value_row_strides;
+  io.q = query;
+  io.key_norm = key_norm;
+  io.key_eps = key_eps;
+  io.bias = logit_bias;
+  io.out_norm = output_norm;
+  io.out_eps = output_eps;
+  io.grad_output = grad_output;
+  io.normed_output = normed_output;
+  io.output_inv_rms = output_inv_rms;
+  io.grad_values = grad_values;
+  io.grad_query = grad_query;
+  io.grad_bias = grad_logit_bias;
+  io.workspace = workspace;
+  e = attnres::base_backward_launch(dtype, plan, io, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_base_backward launch");
+  return ATTNRES_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,121 @@
+// Device helpers shared by the AttnRes read kernels: element types, 16/8/4-byte
+// streaming vector loads, and deterministic lane-group reductions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/attnres_b200.h"
+
+namespace attnres {
+
+constexpr int kMaxSources = ATTNRES_MAX_SOURCES;
+
+// ---------------------------------------------------------------------------
+// element conversion
+// ---------------------------------------------------------------------------
+template <typename T> struct Elem;
+
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+// A VEC-element slice of one row, moved as one aligned memory transaction.
+template <typename T, int VEC> struct alignas(sizeof(T) * VEC) Pack {
+  T e[VEC];
+};
+
+// Read-only streaming load of one pack. Values are read exactly once per
+// kernel, so the 16/8/4-byte forms skip L1 allocation.
+template <typename T, int VEC>
+__device__ __forceinline__ Pack<T, VEC> load_stream(const T* p) {
+  Pack<T, VEC> r;
+  constexpr int B = sizeof(T) * VEC;
+  if constexpr (B == 16) {
+    uint4 u;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                 : "l"(p));
+    *reinterpret_cast<uint4*>(&r) = u;
+  } else if constexpr (B == 8) {
+    uint2 u;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(u.x), "=r"(u.y)
+                 : "l"(p));
+    *reinterpret_cast<uint2*>(&r) = u;
+  } else if constexpr (B == 4) {
+    uint32_t u;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(u) : "l"(p));
+    *reinterpret_cast<uint32_t*>(&r) = u;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) r.e[i] = __ldg(p + i);
+  }
+  return r;
+}
+
+// Plain (L1-cached) load of one pack; used for data that is read again
+// shortly (the upstream gradient, the saved output).
+template <typename T, int VEC>
+__device__ __forceinline__ Pack<T, VEC> load_pack(const T* p) {
+  return *reinterpret_cast<const Pack<T, VEC>*>(p);
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void store_pack(T* p, const float (&x)[VEC]) {
+  Pack<T, VEC> r;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) r.e[i] = Elem<T>::from_f(x[i]);
+  *reinterpret_cast<Pack<T, VEC>*>(p) = r;
+}
+
+template <typename T>
+__device__ __forceinline__ float load_f(const T* p) {
+  return Elem<T>::to_f(__ldg(p));
+}
+
+// ---------------------------------------------------------------------------
+// reductions
+// ---------------------------------------------------------------------------
+// Sum over aligned groups of `g` lanes (g a power of two <= 32). Every lane of
+// the warp must execute the call. The butterfly order is fixed, so the result
+// is deterministic and identical on every lane of the group.
+__device__ __forceinline__ float group_sum(float v, int g) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < g) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__host__ __device__ constexpr int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
+
+inline int next_pow2(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+}  // namespace attnres

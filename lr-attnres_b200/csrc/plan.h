@@ -1,0 +1,111 @@
+// Host/device launch plans and argument bundles of the AttnRes read kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace attnres {
+
+// Thread layout of one LRID launch (computed on the host by make_lrid_plan).
+struct LridPlan {
+  int S, d, R, H, dv, dk;
+  long long N;
+  int vec;    // elements per value pack (16 bytes worth, or 1 for unaligned rows)
+  int nvh;    // packs per head row = dv / vec
+  int tph;    // value threads per head (power of two)
+  int cph;    // packs per value thread = ceil(nvh / tph)
+  int lph;    // key lanes per head (power of two <= 32)
+  int kpl;    // key elements per lane = ceil(dk / lph)
+  int tpt;    // threads per token row (power of two, >= 32)
+  int tpc;    // token rows per CTA
+  int wph;    // warps per head = max(1, tph / 32)
+  int out_norm_group;  // threads in one output-norm reduction group
+  long long ntiles;
+};
+
+struct LridIO {
+  const void* const* values;
+  const int64_t* vstr;
+  const void* const* keys;
+  const int64_t* kstr;
+  int qmode;
+  const void* q;
+  const void* gate;
+  const void* qdyn;
+  float scale;
+  int key_norm;
+  float key_eps;
+  const float* bias;
+  int out_norm;
+  float out_eps;
+  void* out;
+  float* out_inv;
+  float* alpha_out;
+  float* kinv_out;
+};
+
+struct LridGradIO {
+  const void* grad_output;
+  const void* normed_output;
+  const float* output_inv_rms;
+  void* const* grad_values;
+  void* const* grad_keys;
+  void* grad_query;
+  float* grad_gate;
+  void* grad_query_dynamic;
+  float* grad_bias;
+  void* workspace;
+};
+
+// Returns 0 and fills *p, or an attnres_status with a message in *why.
+int make_lrid_plan(int S, long long N, int d, int R, int H, int dtype, bool full_vec, int out_norm,
+                   LridPlan* p, const char** why);
+cudaError_t lrid_workspace(int dtype, const LridPlan& p, size_t* bytes);
+cudaError_t lrid_forward_launch(int dtype, const LridPlan& p, const LridIO& io, cudaStream_t st);
+cudaError_t lrid_backward_launch(int dtype, const LridPlan& p, const LridIO& io,
+                                 const LridGradIO& gio, cudaStream_t st);
+
+// Base AttnRes read (keys are the rms-normed values): one value row of d
+// columns per token, `tpt` threads per token, `cpt` packs per thread.
+struct BasePlan {
+  int S, d;
+  long long N;
+  int vec, nv, tpt, cpt, tpc, wpt;
+  long long ntiles;
+};
+
+struct BaseIO {
+  const void* const* values;
+  const int64_t* vstr;
+  const void* q;
+  int key_norm;
+  float key_eps;
+  const float* bias;
+  int out_norm;
+  float out_eps;
+  void* out;
+  float* out_inv;
+  // backward
+  const void* grad_output;
+  const void* normed_output;
+  const float* output_inv_rms;
+  void* const* grad_values;
+  float* grad_query;
+  float* grad_bias;
+  void* workspace;
+};
+
+int make_base_plan(int S, long long N, int d, int dtype, bool full_vec, BasePlan* p,
+                   const char** why);
+cudaError_t base_workspace(int dtype, const BasePlan& p, size_t* bytes);
+cudaError_t base_forward_launch(int dtype, const BasePlan& p, const BaseIO& io, cudaStream_t st);
+cudaError_t base_backward_launch(int dtype, const BasePlan& p, const BaseIO& io, cudaStream_t st);
+
+}  // namespace attnres
+
+namespace attnres {
+// out[c] = sum over rows r of partials[r*stride + c0 + c], in a fixed order.
+void launch_reduce_partials(const float* partials, int nrows, int stride, int c0, int ncols,
+                            float* out, cudaStream_t st);
+}  // namespace attnres

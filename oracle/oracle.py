@@ -1,0 +1,149 @@
+"""TEST INFRASTRUCTURE ONLY — ctypes wrapper of the C oracle (attnres_oracle.c).
+
+The oracle restates the reference's unfused PyTorch semantics of the block
+Attention-Residual read in double precision (see the citations in
+attnres_oracle.c). Only tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline / reference arm use it, always as the checker or the timed CPU
+baseline, never as part of the product path.
+
+Arrays are numpy; sources are passed stacked and dense: values [S, N, d],
+keys [S, N, R]; query [H, dk] (static / gated), query_dynamic [N, H, dk].
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libattnres_oracle.so")
+
+Q_STATIC, Q_DYNAMIC, Q_GATED = 0, 1, 2
+NORM_NONE, NORM_PER_HEAD, NORM_ROW = 0, 1, 2
+
+_lib = None
+
+
+def build(force=False):
+    src = os.path.join(HERE, "attnres_oracle.c")
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(src) > os.path.getmtime(LIB_PATH):
+        subprocess.run(["make", "-s", "-C", HERE, "-B" if force else "-s"], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.c_void_p
+        I, LL, D = ctypes.c_int, ctypes.c_longlong, ctypes.c_double
+        L.oracle_lrid_forward.argtypes = [I, LL, I, I, I, P, P, I, P, P, P, D, I, D, P, I, D, P, P, P, P]
+        L.oracle_lrid_backward.argtypes = [I, LL, I, I, I, P, P, I, P, P, P, D, I, D, P, I, D, P, P, P, P, P, P, P]
+        L.oracle_base_forward.argtypes = [I, LL, I, P, P, I, D, P, I, D, P, P]
+        L.oracle_base_backward.argtypes = [I, LL, I, P, P, I, D, P, I, D, P, P, P, P]
+        L.oracle_num_threads.restype = I
+        L.oracle_set_num_threads.argtypes = [I]
+        _lib = L
+    return _lib
+
+
+def set_num_threads(n):
+    lib().oracle_set_num_threads(int(n))
+
+
+def num_threads():
+    return lib().oracle_num_threads()
+
+
+def _f32(x):
+    if x is None:
+        return None
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+
+
+def _p(x):
+    return None if x is None else x.ctypes.data_as(ctypes.c_void_p)
+
+
+def _query_args(query, gate, query_dynamic):
+    if query_dynamic is None:
+        return Q_STATIC, _f32(query), None, None
+    if query is None:
+        return Q_DYNAMIC, None, None, _f32(query_dynamic)
+    return Q_GATED, _f32(query), _f32(gate), _f32(query_dynamic)
+
+
+def lrid_forward(values, keys, num_heads, logit_scale, key_norm, query=None, gate=None,
+                 query_dynamic=None, logit_bias=None, output_norm=NORM_NONE,
+                 key_eps=float(np.finfo(np.float32).eps), output_eps=float(np.finfo(np.float32).eps)):
+    """Returns (out [N,d], out_inv, alpha [N,H,S], key_inv_rms [N,H,S]) in float64."""
+    values, keys = _f32(values), _f32(keys)
+    S, N, d = values.shape
+    R = keys.shape[2]
+    H = int(num_heads)
+    qmode, q, g, qd = _query_args(query, gate, query_dynamic)
+    bias = _f32(logit_bias)
+    out = np.zeros((N, d), np.float64)
+    inv = np.zeros((N, H) if output_norm == NORM_PER_HEAD else (N,), np.float64)
+    alpha = np.zeros((N, H, S), np.float64)
+    kinv = np.zeros((N, H, S), np.float64)
+    lib().oracle_lrid_forward(S, N, d, R, H, _p(values), _p(keys), qmode, _p(q), _p(g), _p(qd),
+                              float(logit_scale), int(bool(key_norm)), float(key_eps), _p(bias),
+                              int(output_norm), float(output_eps), _p(out), _p(inv), _p(alpha), _p(kinv))
+    return out, inv, alpha, kinv
+
+
+def lrid_backward(values, keys, num_heads, logit_scale, key_norm, grad_output, query=None, gate=None,
+                  query_dynamic=None, logit_bias=None, output_norm=NORM_NONE,
+                  key_eps=float(np.finfo(np.float32).eps), output_eps=float(np.finfo(np.float32).eps)):
+    """Returns dict with dV [S,N,d], dK [S,N,R], dq, and dgate/dq_dynamic/dbias when relevant."""
+    values, keys, grad_output = _f32(values), _f32(keys), _f32(grad_output)
+    S, N, d = values.shape
+    R = keys.shape[2]
+    H = int(num_heads)
+    qmode, q, g, qd = _query_args(query, gate, query_dynamic)
+    bias = _f32(logit_bias)
+    dV = np.zeros((S, N, d), np.float64)
+    dK = np.zeros((S, N, R), np.float64)
+    dq = np.zeros((N, R) if qmode == Q_DYNAMIC else (R,), np.float64)
+    dgate = np.zeros((H,), np.float64) if qmode == Q_GATED else None
+    dqdyn = np.zeros((N, R), np.float64) if qmode == Q_GATED else None
+    dbias = np.zeros((S,), np.float64) if bias is not None else None
+    lib().oracle_lrid_backward(S, N, d, R, H, _p(values), _p(keys), qmode, _p(q), _p(g), _p(qd),
+                               float(logit_scale), int(bool(key_norm)), float(key_eps), _p(bias),
+                               int(output_norm), float(output_eps), _p(grad_output), _p(dV), _p(dK),
+                               _p(dq), _p(dgate), _p(dqdyn), _p(dbias))
+    res = {"dV": dV, "dK": dK, "dq": dq}
+    if qmode == Q_GATED:
+        res["dgate"] = dgate
+        res["dq_dynamic"] = dqdyn
+    if bias is not None:
+        res["dbias"] = dbias
+    return res
+
+
+def base_forward(values, query, key_norm, logit_bias=None, output_norm=NORM_NONE,
+                 key_eps=float(np.finfo(np.float32).eps), output_eps=float(np.finfo(np.float32).eps)):
+    values, q, bias = _f32(values), _f32(query), _f32(logit_bias)
+    S, N, d = values.shape
+    out = np.zeros((N, d), np.float64)
+    inv = np.zeros((N,), np.float64)
+    lib().oracle_base_forward(S, N, d, _p(values), _p(q), int(bool(key_norm)), float(key_eps), _p(bias),
+                              int(output_norm), float(output_eps), _p(out), _p(inv))
+    return out, inv
+
+
+def base_backward(values, query, key_norm, grad_output, logit_bias=None, output_norm=NORM_NONE,
+                  key_eps=float(np.finfo(np.float32).eps), output_eps=float(np.finfo(np.float32).eps)):
+    values, q, bias, g = _f32(values), _f32(query), _f32(logit_bias), _f32(grad_output)
+    S, N, d = values.shape
+    dV = np.zeros((S, N, d), np.float64)
+    dq = np.zeros((d,), np.float64)
+    dbias = np.zeros((S,), np.float64) if bias is not None else None
+    lib().oracle_base_backward(S, N, d, _p(values), _p(q), int(bool(key_norm)), float(key_eps), _p(bias),
+                               int(output_norm), float(output_eps), _p(g), _p(dV), _p(dq), _p(dbias))
+    res = {"dV": dV, "dq": dq}
+    if bias is not None:
+        res["dbias"] = dbias
+    return res
