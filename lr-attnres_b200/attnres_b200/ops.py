@@ -1,0 +1,700 @@
+"""torch.library operators and public read functions over libattnres_b200.
+
+Mirrors the reference's op layer (attnres_ops.py of jon123boss/LR-AttnRes):
+
+  attnres::lrid_read_list / attnres::lrid_read_list_backward
+      same names, schemas and outputs as attnres_ops.py:4636-4802, including
+      register_autograd (attnres_ops.py:4805-4847).
+  attnres::lrid_read / attnres::lrid_read_backward
+      the general LRID read used by the public function: static, dynamic or
+      gated-hybrid query (model.py:2102-2115), per-source logit biases
+      (attnres_ops.py:84-105), and output RMS norm per head or per row.
+  attnres::base_read / attnres::base_read_backward
+      the base AttnRes read (attnres_ops.py:2301-2421).
+  lrid_attention_residual_read(...)   signature of attnres_ops.py:4852
+  attention_residual_read(...)        signature of attnres_ops.py:2503
+
+Every tensor argument must live on a CUDA device; the work is enqueued on the
+current stream through the C ABI. There is no CPU fallback: a CPU tensor is a
+RuntimeError.
+"""
+import ctypes
+from typing import List, Optional, Sequence
+
+import torch
+from torch import Tensor
+from torch.nn import functional as F
+
+from . import _native as N
+
+F32_EPS = float(torch.finfo(torch.float32).eps)
+
+_DTYPES = {torch.float32: N.DTYPE_F32, torch.float16: N.DTYPE_F16, torch.bfloat16: N.DTYPE_BF16}
+
+
+def _dtype_code(dt):
+    try:
+        return _DTYPES[dt]
+    except KeyError:
+        raise RuntimeError(f"attnres_b200: unsupported dtype {dt}; use float32, float16 or bfloat16") from None
+
+
+def _require_cuda(tensors, what):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                f"attnres_b200: {what} must be CUDA tensors (the fused read has no CPU path)"
+            )
+
+
+def _stream_ptr(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _row_view(t: Tensor, width: int):
+    """A token-row view of a [B, T, width] / [N, width] source: returns the
+    tensor (made dense in its last dim if needed) and its row stride."""
+    if t.size(-1) != width:
+        raise RuntimeError(f"attnres_b200: source last dim {t.size(-1)} != {width}")
+    if t.dim() == 3:
+        if t.stride(-1) != 1 or t.stride(0) != t.size(1) * t.stride(1):
+            t = t.contiguous()
+        return t, (t.stride(1) if t.size(1) > 1 or t.size(0) > 1 else width)
+    if t.dim() == 2:
+        if t.stride(-1) != 1:
+            t = t.contiguous()
+        return t, (t.stride(0) if t.size(0) > 1 else width)
+    raise RuntimeError("attnres_b200: sources must be [B, T, C] or [N, C]")
+
+
+def _sources(tensors: Sequence[Tensor], width: int, dtype):
+    rows, strides = [], []
+    for t in tensors:
+        if t.dtype != dtype:
+            raise RuntimeError("attnres_b200: all sources of a read must share one dtype")
+        t, st = _row_view(t, width)
+        rows.append(t)
+        strides.append(max(int(st), width))
+    return rows, strides
+
+
+def _ntok(t: Tensor):
+    return t.numel() // t.size(-1)
+
+
+def _lead_shape(t: Tensor):
+    return tuple(t.shape[:-1])
+
+
+def _output_norm_mode(normalize_output: bool, num_heads: int) -> int:
+    """The reference fuses the output norm per head when H == 1 and otherwise
+    RMS-normalises the whole output row (attnres_ops.py:4871, :4985)."""
+    if not normalize_output:
+        return N.NORM_NONE
+    return N.NORM_PER_HEAD if int(num_heads) == 1 else N.NORM_ROW
+
+
+# ---------------------------------------------------------------------------
+# raw launchers (no autograd)
+# ---------------------------------------------------------------------------
+def _lrid_forward_impl(values, keys, query, query_gate, query_dynamic, logit_bias, num_heads,
+                       logit_scale, key_norm, output_norm, save_aux):
+    S = len(values)
+    if S < 1 or len(keys) != S:
+        raise RuntimeError("attnres_b200: need one key tensor per value source (S >= 1)")
+    if S > N.MAX_SOURCES:
+        raise RuntimeError(f"attnres_b200: at most {N.MAX_SOURCES} sources per read")
+    _require_cuda([*values, *keys, query, query_gate, query_dynamic, logit_bias], "LRID read inputs")
+    H = int(num_heads)
+    d = values[0].size(-1)
+    R = keys[0].size(-1)
+    if H < 1 or d % H or R % H:
+        raise RuntimeError(f"attnres_b200: value dim {d} and key dim {R} must divide by num_heads {H}")
+    dtype = values[0].dtype
+    code = _dtype_code(dtype)
+    vrows, vstr = _sources(values, d, dtype)
+    krows, kstr = _sources(keys, R, dtype)
+    n = _ntok(values[0])
+    device = values[0].device
+    qmode, q, g, qd = _query_pack(query, query_gate, query_dynamic, H, R, n, dtype)
+    bias = None if logit_bias is None else logit_bias.to(torch.float32).reshape(-1).contiguous()
+    if bias is not None and bias.numel() != S:
+        raise RuntimeError("source_logit_biases length must match the number of sources")
+    out = torch.empty((*_lead_shape(values[0]), d), device=device, dtype=dtype)
+    if output_norm == N.NORM_PER_HEAD:
+        out_inv = torch.empty((n, H), device=device, dtype=torch.float32)
+    elif output_norm == N.NORM_ROW:
+        out_inv = torch.empty((n,), device=device, dtype=torch.float32)
+    else:
+        out_inv = torch.empty((1,), device=device, dtype=torch.float32)
+    if save_aux:
+        alpha = torch.empty((n, H, S), device=device, dtype=torch.float32)
+        kinv = torch.empty((n, H, S), device=device, dtype=torch.float32)
+    else:
+        alpha = torch.empty((1,), device=device, dtype=torch.float32)
+        kinv = torch.empty((1,), device=device, dtype=torch.float32)
+    with torch.cuda.device(device):
+        rc = N.load().attnres_lrid_forward(
+            S, n, d, R, H, code,
+            N.ptr_array([t.data_ptr() for t in vrows]), N.i64_array(vstr),
+            N.ptr_array([t.data_ptr() for t in krows]), N.i64_array(kstr),
+            qmode, _ptr(q), _ptr(g), _ptr(qd),
+            float(logit_scale), int(bool(key_norm)), F32_EPS, _ptr(bias),
+            int(output_norm), float(torch.finfo(dtype).eps),
+            _ptr(out), _ptr(out_inv) if output_norm != N.NORM_NONE else None,
+            _ptr(alpha) if save_aux else None, _ptr(kinv) if save_aux else None,
+            _stream_ptr(device),
+        )
+    N.check(rc, "attnres_lrid_forward")
+    return out, out_inv, alpha, kinv
+
+
+def _query_pack(query, gate, query_dynamic, H, R, n, dtype):
+    dk = R // H
+    if query_dynamic is not None:
+        qd = query_dynamic.to(dtype).reshape(n, H, dk).contiguous()
+        if query is None:
+            return N.QUERY_DYNAMIC, None, None, qd
+        if gate is None:
+            raise RuntimeError("attnres_b200: a gated query needs query_gate")
+        q = query.to(dtype).reshape(H, dk).contiguous()
+        g = gate.to(dtype).reshape(H).contiguous()
+        return N.QUERY_GATED, q, g, qd
+    if query is None:
+        raise RuntimeError("attnres_b200: query is required")
+    if query.dim() == 4:
+        return N.QUERY_DYNAMIC, None, None, query.to(dtype).reshape(n, H, dk).contiguous()
+    if query.numel() != R:
+        raise RuntimeError(f"attnres_b200: static query must have {R} elements ([H, R/H])")
+    return N.QUERY_STATIC, query.to(dtype).reshape(H, dk).contiguous(), None, None
+
+
+def _lrid_backward_impl(values, keys, query, query_gate, query_dynamic, logit_bias, grad_output,
+                        normed_output, output_inv_rms, num_heads, logit_scale, key_norm,
+                        output_norm, need_bias_grad=True):
+    S = len(values)
+    H = int(num_heads)
+    d = values[0].size(-1)
+    R = keys[0].size(-1)
+    dtype = values[0].dtype
+    code = _dtype_code(dtype)
+    _require_cuda([*values, *keys, query, query_gate, query_dynamic, logit_bias, grad_output],
+                  "LRID read backward inputs")
+    vrows, vstr = _sources(values, d, dtype)
+    krows, kstr = _sources(keys, R, dtype)
+    n = _ntok(values[0])
+    device = values[0].device
+    qmode, q, g, qd = _query_pack(query, query_gate, query_dynamic, H, R, n, dtype)
+    bias = None if logit_bias is None else logit_bias.to(torch.float32).reshape(-1).contiguous()
+    grad_output = grad_output.to(dtype).reshape(n, d).contiguous()
+    y = None
+    if output_norm != N.NORM_NONE:
+        y = normed_output.to(dtype).reshape(n, d).contiguous()
+        output_inv_rms = output_inv_rms.to(torch.float32).contiguous()
+    grad_values = [torch.empty((*_lead_shape(v), d), device=device, dtype=dtype) for v in values]
+    grad_keys = [torch.empty((*_lead_shape(k), R), device=device, dtype=dtype) for k in keys]
+    if qmode == N.QUERY_DYNAMIC:
+        dq = torch.empty((n, H, R // H), device=device, dtype=dtype)
+    else:
+        dq = torch.empty((H, R // H), device=device, dtype=torch.float32)
+    dgate = torch.empty((H,), device=device, dtype=torch.float32) if qmode == N.QUERY_GATED else None
+    dqd = torch.empty((n, H, R // H), device=device, dtype=dtype) if qmode == N.QUERY_GATED else None
+    dbias = torch.empty((S,), device=device, dtype=torch.float32) if (bias is not None and need_bias_grad) else None
+    with torch.cuda.device(device):
+        L = N.load()
+        ws_bytes = L.attnres_lrid_backward_workspace_bytes(S, n, d, R, H, code)
+        ws = torch.empty((max(16, ws_bytes),), device=device, dtype=torch.uint8)
+        rc = L.attnres_lrid_backward(
+            S, n, d, R, H, code,
+            N.ptr_array([t.data_ptr() for t in vrows]), N.i64_array(vstr),
+            N.ptr_array([t.data_ptr() for t in krows]), N.i64_array(kstr),
+            qmode, _ptr(q), _ptr(g), _ptr(qd),
+            float(logit_scale), int(bool(key_norm)), F32_EPS, _ptr(bias),
+            int(output_norm), float(torch.finfo(dtype).eps),
+            _ptr(grad_output), _ptr(y), _ptr(output_inv_rms) if y is not None else None,
+            N.ptr_array([t.data_ptr() for t in grad_values]),
+            N.ptr_array([t.data_ptr() for t in grad_keys]),
+            _ptr(dq), _ptr(dgate), _ptr(dqd), _ptr(dbias),
+            _ptr(ws), ws.numel(), _stream_ptr(device),
+        )
+    N.check(rc, "attnres_lrid_backward")
+    return grad_values, grad_keys, dq, dgate, dqd, dbias
+
+
+# ---------------------------------------------------------------------------
+# attnres::lrid_read_list — reference-compatible library op
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("attnres::lrid_read_list", mutates_args=())
+def lrid_read_list(
+    values: List[Tensor],
+    keys: List[Tensor],
+    query: Tensor,
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    normalize_output: bool,
+    save_aux: bool,
+) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Reference attnres_ops.py:4636. normalize_output normalises each head."""
+    norm = N.NORM_PER_HEAD if normalize_output else N.NORM_NONE
+    out, inv, alpha, kinv = _lrid_forward_impl(
+        list(values), list(keys), query, None, None, None, num_heads, logit_scale, key_norm,
+        norm, save_aux,
+    )
+    return out, inv, alpha, kinv
+
+
+@lrid_read_list.register_fake
+def _(values, keys, query, num_heads, logit_scale, key_norm, normalize_output, save_aux):
+    v0 = values[0]
+    n = v0.numel() // v0.size(-1)
+    H, S = int(num_heads), len(values)
+    out = v0.new_empty(v0.shape)
+    inv = v0.new_empty((n, H) if normalize_output else (1,), dtype=torch.float32)
+    aux = (n, H, S) if save_aux else (1,)
+    return out, inv, v0.new_empty(aux, dtype=torch.float32), v0.new_empty(aux, dtype=torch.float32)
+
+
+@torch.library.custom_op("attnres::lrid_read_list_backward", mutates_args=())
+def lrid_read_list_backward(
+    values: List[Tensor],
+    keys: List[Tensor],
+    query: Tensor,
+    grad_output: Tensor,
+    normed_output: Tensor,
+    output_inv_rms: Tensor,
+    alpha_saved: Tensor,
+    key_inv_rms_saved: Tensor,
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    normalize_output: bool,
+    use_aux: bool,
+) -> tuple[List[Tensor], List[Tensor], Tensor]:
+    """Reference attnres_ops.py:4725. The softmax weights are recomputed from the
+    keys with the forward's arithmetic, so `alpha_saved` / `key_inv_rms_saved`
+    (use_aux) are accepted for interface parity and give identical results."""
+    norm = N.NORM_PER_HEAD if normalize_output else N.NORM_NONE
+    gv, gk, dq, _, _, _ = _lrid_backward_impl(
+        list(values), list(keys), query, None, None, None, grad_output, normed_output,
+        output_inv_rms, num_heads, logit_scale, key_norm, norm,
+    )
+    return gv, gk, dq.reshape(query.shape).to(query.dtype)
+
+
+@lrid_read_list_backward.register_fake
+def _(values, keys, query, grad_output, normed_output, output_inv_rms, alpha_saved,
+      key_inv_rms_saved, num_heads, logit_scale, key_norm, normalize_output, use_aux):
+    return ([v.new_empty(v.shape) for v in values], [k.new_empty(k.shape) for k in keys],
+            query.new_empty(query.shape))
+
+
+def _lrid_read_list_setup(ctx, inputs, output):
+    values, keys, query, num_heads, logit_scale, key_norm, normalize_output, save_aux = inputs
+    out, inv, alpha, kinv = output
+    ctx.save_for_backward(query, out, inv, alpha, kinv, *values, *keys)
+    ctx.num_sources = len(values)
+    ctx.num_heads = int(num_heads)
+    ctx.logit_scale = float(logit_scale)
+    ctx.key_norm = bool(key_norm)
+    ctx.normalize_output = bool(normalize_output)
+    ctx.use_aux = bool(save_aux)
+
+
+def _lrid_read_list_bwd(ctx, grad_out, grad_inv, grad_alpha, grad_kinv):
+    saved = ctx.saved_tensors
+    query, out, inv, alpha, kinv = saved[:5]
+    values = list(saved[5:5 + ctx.num_sources])
+    keys = list(saved[5 + ctx.num_sources:])
+    gv, gk, dq = lrid_read_list_backward(
+        values, keys, query, grad_out, out, inv, alpha, kinv, ctx.num_heads, ctx.logit_scale,
+        ctx.key_norm, ctx.normalize_output, ctx.use_aux,
+    )
+    return gv, gk, dq, None, None, None, None, None
+
+
+lrid_read_list.register_autograd(_lrid_read_list_bwd, setup_context=_lrid_read_list_setup)
+
+
+# ---------------------------------------------------------------------------
+# attnres::lrid_read — general LRID read (gated query, logit bias, row norm)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("attnres::lrid_read", mutates_args=())
+def lrid_read(
+    values: List[Tensor],
+    keys: List[Tensor],
+    query: Optional[Tensor],
+    query_gate: Optional[Tensor],
+    query_dynamic: Optional[Tensor],
+    logit_bias: Optional[Tensor],
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    output_norm: int,
+) -> tuple[Tensor, Tensor]:
+    out, inv, _, _ = _lrid_forward_impl(
+        list(values), list(keys), query, query_gate, query_dynamic, logit_bias, num_heads,
+        logit_scale, key_norm, int(output_norm), False,
+    )
+    return out, inv
+
+
+@lrid_read.register_fake
+def _(values, keys, query, query_gate, query_dynamic, logit_bias, num_heads, logit_scale,
+      key_norm, output_norm):
+    v0 = values[0]
+    n = v0.numel() // v0.size(-1)
+    shape = {N.NORM_PER_HEAD: (n, int(num_heads)), N.NORM_ROW: (n,)}.get(int(output_norm), (1,))
+    return v0.new_empty(v0.shape), v0.new_empty(shape, dtype=torch.float32)
+
+
+@torch.library.custom_op("attnres::lrid_read_backward", mutates_args=())
+def lrid_read_backward(
+    values: List[Tensor],
+    keys: List[Tensor],
+    query: Optional[Tensor],
+    query_gate: Optional[Tensor],
+    query_dynamic: Optional[Tensor],
+    logit_bias: Optional[Tensor],
+    grad_output: Tensor,
+    normed_output: Tensor,
+    output_inv_rms: Tensor,
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    output_norm: int,
+) -> tuple[List[Tensor], List[Tensor], Tensor, Tensor, Tensor, Tensor]:
+    """Returns (dV list, dK list, dq, dgate, dq_dynamic, dbias); dq is fp32 [H, dk]
+    for a static/gated query and [N, H, dk] in the value dtype for a dynamic one;
+    absent gradients are returned as empty tensors."""
+    gv, gk, dq, dgate, dqd, dbias = _lrid_backward_impl(
+        list(values), list(keys), query, query_gate, query_dynamic, logit_bias, grad_output,
+        normed_output, output_inv_rms, num_heads, logit_scale, key_norm, int(output_norm),
+    )
+    e = values[0].new_empty((0,), dtype=torch.float32)
+    return (gv, gk, dq, dgate if dgate is not None else e, dqd if dqd is not None else e.clone(),
+            dbias if dbias is not None else e.clone())
+
+
+@lrid_read_backward.register_fake
+def _(values, keys, query, query_gate, query_dynamic, logit_bias, grad_output, normed_output,
+      output_inv_rms, num_heads, logit_scale, key_norm, output_norm):
+    v0 = values[0]
+    n = v0.numel() // v0.size(-1)
+    H, R = int(num_heads), keys[0].size(-1)
+    e = v0.new_empty((0,), dtype=torch.float32)
+    if query_dynamic is not None and query is None:
+        dq = v0.new_empty((n, H, R // H))
+    else:
+        dq = v0.new_empty((H, R // H), dtype=torch.float32)
+    gated = query_dynamic is not None and query is not None
+    return ([v.new_empty(v.shape) for v in values], [k.new_empty(k.shape) for k in keys], dq,
+            v0.new_empty((H,), dtype=torch.float32) if gated else e,
+            v0.new_empty((n, H, R // H)) if gated else e.clone(),
+            v0.new_empty((len(values),), dtype=torch.float32) if logit_bias is not None else e.clone())
+
+
+def _lrid_read_setup(ctx, inputs, output):
+    values, keys, query, gate, qdyn, bias, num_heads, logit_scale, key_norm, output_norm = inputs
+    out, inv = output
+    ctx.has = (query is not None, gate is not None, qdyn is not None, bias is not None)
+    opt = [x for x in (query, gate, qdyn, bias) if x is not None]
+    ctx.save_for_backward(out, inv, *opt, *values, *keys)
+    ctx.num_sources = len(values)
+    ctx.n_opt = len(opt)
+    ctx.args = (int(num_heads), float(logit_scale), bool(key_norm), int(output_norm))
+
+
+def _lrid_read_bwd(ctx, grad_out, grad_inv):
+    saved = list(ctx.saved_tensors)
+    out, inv = saved[0], saved[1]
+    opt = iter(saved[2:2 + ctx.n_opt])
+    query, gate, qdyn, bias = (next(opt) if h else None for h in ctx.has)
+    rest = saved[2 + ctx.n_opt:]
+    values, keys = list(rest[:ctx.num_sources]), list(rest[ctx.num_sources:])
+    H, scale, key_norm, output_norm = ctx.args
+    gv, gk, dq, dgate, dqd, dbias = lrid_read_backward(
+        values, keys, query, gate, qdyn, bias, grad_out, out, inv, H, scale, key_norm, output_norm,
+    )
+    g_query = g_gate = g_qdyn = g_bias = None
+    if qdyn is not None and query is None:
+        g_qdyn = dq.reshape(qdyn.shape).to(qdyn.dtype)
+    else:
+        g_query = dq.reshape(query.shape).to(query.dtype)
+        if qdyn is not None:
+            g_gate = dgate.reshape(gate.shape).to(gate.dtype)
+            g_qdyn = dqd.reshape(qdyn.shape).to(qdyn.dtype)
+    if bias is not None:
+        g_bias = dbias.reshape(bias.shape).to(bias.dtype)
+    return gv, gk, g_query, g_gate, g_qdyn, g_bias, None, None, None, None
+
+
+lrid_read.register_autograd(_lrid_read_bwd, setup_context=_lrid_read_setup)
+
+
+# ---------------------------------------------------------------------------
+# attnres::base_read — base AttnRes read (keys are rms-normed values)
+# ---------------------------------------------------------------------------
+def _base_forward_impl(values, query, logit_bias, key_norm, normalize_output):
+    S = len(values)
+    if S < 1 or S > N.MAX_SOURCES:
+        raise RuntimeError(f"attnres_b200: base read needs 1..{N.MAX_SOURCES} sources")
+    _require_cuda([*values, query, logit_bias], "base read inputs")
+    d = values[0].size(-1)
+    dtype = values[0].dtype
+    code = _dtype_code(dtype)
+    rows, strides = _sources(values, d, dtype)
+    n = _ntok(values[0])
+    device = values[0].device
+    q = query.to(dtype).reshape(d).contiguous()
+    bias = None if logit_bias is None else logit_bias.to(torch.float32).reshape(-1).contiguous()
+    eps = float(torch.finfo(dtype).eps)
+    out = torch.empty((*_lead_shape(values[0]), d), device=device, dtype=dtype)
+    inv = torch.empty((n,) if normalize_output else (1,), device=device, dtype=torch.float32)
+    with torch.cuda.device(device):
+        rc = N.load().attnres_base_forward(
+            S, n, d, code, N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            _ptr(q), int(bool(key_norm)), eps, _ptr(bias),
+            N.NORM_ROW if normalize_output else N.NORM_NONE, eps,
+            _ptr(out), _ptr(inv) if normalize_output else None, _stream_ptr(device),
+        )
+    N.check(rc, "attnres_base_forward")
+    return out, inv
+
+
+@torch.library.custom_op("attnres::base_read", mutates_args=())
+def base_read(
+    values: List[Tensor],
+    query: Tensor,
+    logit_bias: Optional[Tensor],
+    key_norm: bool,
+    normalize_output: bool,
+) -> tuple[Tensor, Tensor]:
+    return _base_forward_impl(list(values), query, logit_bias, key_norm, normalize_output)
+
+
+@base_read.register_fake
+def _(values, query, logit_bias, key_norm, normalize_output):
+    v0 = values[0]
+    n = v0.numel() // v0.size(-1)
+    return v0.new_empty(v0.shape), v0.new_empty((n,) if normalize_output else (1,), dtype=torch.float32)
+
+
+@torch.library.custom_op("attnres::base_read_backward", mutates_args=())
+def base_read_backward(
+    values: List[Tensor],
+    query: Tensor,
+    logit_bias: Optional[Tensor],
+    grad_output: Tensor,
+    normed_output: Tensor,
+    output_inv_rms: Tensor,
+    key_norm: bool,
+    normalize_output: bool,
+) -> tuple[List[Tensor], Tensor, Tensor]:
+    values = list(values)
+    S = len(values)
+    d = values[0].size(-1)
+    dtype = values[0].dtype
+    code = _dtype_code(dtype)
+    _require_cuda([*values, query, grad_output], "base read backward inputs")
+    rows, strides = _sources(values, d, dtype)
+    n = _ntok(values[0])
+    device = values[0].device
+    q = query.to(dtype).reshape(d).contiguous()
+    bias = None if logit_bias is None else logit_bias.to(torch.float32).reshape(-1).contiguous()
+    eps = float(torch.finfo(dtype).eps)
+    g = grad_output.to(dtype).reshape(n, d).contiguous()
+    y = normed_output.to(dtype).reshape(n, d).contiguous() if normalize_output else None
+    inv = output_inv_rms.to(torch.float32).contiguous() if normalize_output else None
+    gv = [torch.empty((*_lead_shape(v), d), device=device, dtype=dtype) for v in values]
+    dq = torch.empty((d,), device=device, dtype=torch.float32)
+    dbias = torch.empty((S,), device=device, dtype=torch.float32) if bias is not None else None
+    with torch.cuda.device(device):
+        L = N.load()
+        ws_bytes = L.attnres_base_backward_workspace_bytes(S, n, d, code)
+        ws = torch.empty((max(16, ws_bytes),), device=device, dtype=torch.uint8)
+        rc = L.attnres_base_backward(
+            S, n, d, code, N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            _ptr(q), int(bool(key_norm)), eps, _ptr(bias),
+            N.NORM_ROW if normalize_output else N.NORM_NONE, eps,
+            _ptr(g), _ptr(y), _ptr(inv), N.ptr_array([t.data_ptr() for t in gv]),
+            _ptr(dq), _ptr(dbias), _ptr(ws), ws.numel(), _stream_ptr(device),
+        )
+    N.check(rc, "attnres_base_backward")
+    e = values[0].new_empty((0,), dtype=torch.float32)
+    return gv, dq.reshape(query.shape).to(query.dtype), dbias if dbias is not None else e
+
+
+@base_read_backward.register_fake
+def _(values, query, logit_bias, grad_output, normed_output, output_inv_rms, key_norm,
+      normalize_output):
+    e = values[0].new_empty((0,), dtype=torch.float32)
+    db = values[0].new_empty((len(values),), dtype=torch.float32) if logit_bias is not None else e
+    return [v.new_empty(v.shape) for v in values], query.new_empty(query.shape), db
+
+
+def _base_read_setup(ctx, inputs, output):
+    values, query, bias, key_norm, normalize_output = inputs
+    out, inv = output
+    ctx.has_bias = bias is not None
+    ctx.save_for_backward(out, inv, query, *([bias] if bias is not None else []), *values)
+    ctx.args = (bool(key_norm), bool(normalize_output))
+
+
+def _base_read_bwd(ctx, grad_out, grad_inv):
+    saved = list(ctx.saved_tensors)
+    out, inv, query = saved[:3]
+    bias = saved[3] if ctx.has_bias else None
+    values = saved[4 if ctx.has_bias else 3:]
+    key_norm, normalize_output = ctx.args
+    gv, dq, dbias = base_read_backward(values, query, bias, grad_out, out, inv, key_norm, normalize_output)
+    g_bias = dbias.reshape(bias.shape).to(bias.dtype) if bias is not None else None
+    return gv, dq, g_bias, None, None
+
+
+base_read.register_autograd(_base_read_bwd, setup_context=_base_read_setup)
+
+
+# ---------------------------------------------------------------------------
+# public functions (signatures of the reference's attnres_ops.py)
+# ---------------------------------------------------------------------------
+def _norm(x: Tensor) -> Tensor:
+    return F.rms_norm(x, (x.size(-1),))
+
+
+def source_logit_bias(source_counts, source_logit_biases, n_sources: int, device) -> Optional[Tensor]:
+    """Per-source fp32 logit bias: log(count) for `source_counts`, or the given
+    (possibly learned) biases. Same rules and errors as attnres_ops.py:61-105."""
+    if source_counts is not None and source_logit_biases is not None:
+        raise RuntimeError("source_counts and source_logit_biases are mutually exclusive")
+    if source_logit_biases is None:
+        if source_counts is None:
+            return None
+        if isinstance(source_counts, Tensor):
+            counts = source_counts.reshape(-1).to(device=device, dtype=torch.float32)
+        elif isinstance(source_counts, (int, float)):
+            counts = torch.full((n_sources,), float(source_counts), device=device, dtype=torch.float32)
+        else:
+            if len(source_counts) != n_sources:
+                raise RuntimeError("source_counts length must match the number of sources")
+            vals = [float(c) for c in source_counts]
+            if any(c <= 0.0 for c in vals):
+                raise RuntimeError("source_counts must be positive")
+            counts = torch.tensor(vals, device=device, dtype=torch.float32)
+        if counts.numel() != n_sources:
+            raise RuntimeError("source_counts length must match the number of sources")
+        return counts.log()
+    if isinstance(source_logit_biases, Tensor):
+        biases = source_logit_biases.reshape(-1).to(device=device, dtype=torch.float32)
+    elif isinstance(source_logit_biases, (int, float)):
+        biases = torch.full((n_sources,), float(source_logit_biases), device=device, dtype=torch.float32)
+    else:
+        if len(source_logit_biases) != n_sources:
+            raise RuntimeError("source_logit_biases length must match the number of sources")
+        biases = torch.stack([
+            b.to(device=device, dtype=torch.float32).reshape(())
+            if isinstance(b, Tensor) else torch.tensor(float(b), device=device, dtype=torch.float32)
+            for b in source_logit_biases
+        ])
+    if biases.numel() != n_sources:
+        raise RuntimeError("source_logit_biases length must match the number of sources")
+    return biases
+
+
+def _as_list(x):
+    return list(x.unbind(0)) if isinstance(x, Tensor) else list(x)
+
+
+def lrid_attention_residual_read(
+    values,
+    keys,
+    query: Tensor,
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    force_triton: bool = False,
+    normalize_output: bool = False,
+    source_counts=None,
+    source_logit_biases=None,
+) -> Tensor:
+    """LR-AttnRes read (reference attnres_ops.py:4852). `values`/`keys` are lists
+    (or stacked [S, ...] tensors) of [B, T, d] / [B, T, R]; `query` is static
+    [H, R/H] or dynamic [B, T, H, R/H]. `force_triton` is accepted for signature
+    compatibility; the fused CUDA path is the only path."""
+    values, keys = _as_list(values), _as_list(keys)
+    query = query.to(keys[0].dtype)
+    if len(values) == 1:
+        return _norm(values[0]) if normalize_output else values[0]
+    if keys[0].dtype != values[0].dtype:
+        keys = [k.to(values[0].dtype) for k in keys]
+    bias = source_logit_bias(source_counts, source_logit_biases, len(values), values[0].device)
+    norm = _output_norm_mode(normalize_output, num_heads)
+    if query.dim() == 4:
+        out, _ = lrid_read(values, keys, None, None, query, bias, int(num_heads), float(logit_scale),
+                           bool(key_norm), norm)
+    else:
+        out, _ = lrid_read(values, keys, query, None, None, bias, int(num_heads), float(logit_scale),
+                           bool(key_norm), norm)
+    return out
+
+
+def lrid_attention_residual_read_gated(
+    values,
+    keys,
+    static_query: Tensor,
+    query_gate: Tensor,
+    dynamic_query: Tensor,
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    normalize_output: bool = False,
+    source_counts=None,
+    source_logit_biases=None,
+) -> Tensor:
+    """LR-AttnRes read with the input-dependent gated hybrid query
+    q_t = static_query + query_gate * dynamic_query_t (model.py:2104-2110), formed
+    inside the kernel. Gradients flow to all three query tensors."""
+    values, keys = _as_list(values), _as_list(keys)
+    dtype = keys[0].dtype
+    if len(values) == 1:
+        return _norm(values[0]) if normalize_output else values[0]
+    if keys[0].dtype != values[0].dtype:
+        keys = [k.to(values[0].dtype) for k in keys]
+    bias = source_logit_bias(source_counts, source_logit_biases, len(values), values[0].device)
+    norm = _output_norm_mode(normalize_output, num_heads)
+    out, _ = lrid_read(values, keys, static_query.to(dtype), query_gate.to(dtype), dynamic_query.to(dtype),
+                       bias, int(num_heads), float(logit_scale), bool(key_norm), norm)
+    return out
+
+
+def attention_residual_read(
+    values,
+    query: Tensor,
+    key_norm: bool,
+    force_triton: bool = False,
+    normalize_output: bool = False,
+    source_counts=None,
+    source_logit_biases=None,
+) -> Tensor:
+    """Base AttnRes read (reference attnres_ops.py:2503): keys are the rms-normed
+    values, logits <key, query> (+ per-source bias), softmax over sources."""
+    values = _as_list(values)
+    if len(values) == 1:
+        return _norm(values[0]) if normalize_output else values[0]
+    query = query.to(values[0].dtype)
+    bias = source_logit_bias(source_counts, source_logit_biases, len(values), values[0].device)
+    out, _ = base_read(values, query, bias, bool(key_norm), bool(normalize_output))
+    return out
+
+
+def is_fused_attnres_available() -> bool:
+    """True when the CUDA library loads and a CUDA device is present."""
+    try:
+        N.load()
+    except N.AttnResError:
+        return False
+    return torch.cuda.is_available()
