@@ -235,33 +235,35 @@ def test_lrid_backward_is_deterministic():
 
 
 def test_lrid_query_grad_is_additive_over_token_shards():
-    """Size-independent property at the full BASELINE config-2 size: the summed
+    """Size-independent property at the full BASELINE config-2 size: the fp32
     query gradient of the whole batch equals the sum over token shards (each
     shard run on its own), and the per-token outputs equal the oracle on a
-    slice at each end of the batch."""
-    ops = _ops()
+    slice at each end of the batch. Calls the attnres::lrid_read ops directly,
+    so dq is compared before the cast to the bf16 query dtype."""
+    ops = torch.ops.attnres
+    _ops()
     S, B, T, D, R, H = 9, 8, 2048, 1024, 64, 1
     torch.manual_seed(1)
     values = [torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
     keys = [torch.randn(B, T, R, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
-    q0 = torch.randn(H, R // H, device="cuda") * 0.02
+    q0 = (torch.randn(H, R // H, device="cuda") * 0.02).to(torch.bfloat16)
     g = torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16)
 
     def run(sl):
-        vs = [v[sl].detach().requires_grad_(True) for v in values]
-        ks = [k[sl].detach().requires_grad_(True) for k in keys]
-        q = q0.clone().requires_grad_(True)
-        out = ops.lrid_attention_residual_read(vs, ks, q, H, 0.125, True)
-        out.backward(g[sl])
-        return out, q.grad.double()
+        vs = [v[sl] for v in values]
+        ks = [k[sl] for k in keys]
+        out, inv = ops.lrid_read(vs, ks, q0, None, None, None, H, 0.125, True, 0)
+        res = ops.lrid_read_backward(vs, ks, q0, None, None, None, g[sl], out, inv, H, 0.125, True, 0)
+        return out, res[2].double()
 
     out_full, dq_full = run(slice(0, B))
     dq_sum = sum(run(slice(i, i + 2))[1] for i in range(0, B, 2))
-    torch.testing.assert_close(dq_full, dq_sum, rtol=1e-4, atol=1e-4 * float(dq_full.abs().max()))
+    # fp32 partial sums over 16384 tokens x 9 sources: allow 1e-5 of the scale
+    torch.testing.assert_close(dq_full, dq_sum, rtol=1e-5, atol=1e-5 * float(dq_full.abs().max()))
     for sl in (slice(0, 1), slice(B - 1, B)):
         v = np.stack([to_np(x[sl]).reshape(-1, D) for x in values])
         k = np.stack([to_np(x[sl]).reshape(-1, R) for x in keys])
-        ref = oracle.lrid_forward(v, k, H, 0.125, True, query=rounded(to_np(q0), torch.bfloat16))[0]
+        ref = oracle.lrid_forward(v, k, H, 0.125, True, query=to_np(q0))[0]
         assert_close("out", to_np(out_full[sl]).reshape(-1, D), ref, torch.bfloat16)
 
 
