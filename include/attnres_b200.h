@@ -80,6 +80,17 @@ int attnres_abi_version(void);
 const char* attnres_last_error(void);
 
 /*
+ * Health word of the bulk-copy kernels on the current device. A kernel that
+ * waits on a shared-memory pipeline barrier gives up after ~2 s instead of
+ * hanging, sets a bit here and returns (its outputs are then invalid):
+ *   1 = consumers timed out waiting for a stage, 2 = producer timed out
+ *   waiting for a stage to drain, 4 = producer timed out draining its copies.
+ * Synchronous (reads device memory). reset != 0 clears the word afterwards.
+ * No reference counterpart (the reference's Triton kernels have no waits).
+ */
+int attnres_device_status(unsigned* status, int reset);
+
+/*
  * LRID read, forward. Replaces attnres::lrid_read_list (attnres_ops.py:4636).
  *   logit[n,h,s] = logit_scale * <khat[s,n,h,:], q[n,h,:]> + logit_bias[s]
  *   khat         = key_norm ? k * rsqrt(mean(k^2) + key_eps) : k     (per head of dk)

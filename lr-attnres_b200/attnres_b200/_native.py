@@ -25,6 +25,7 @@ STATUS_NAMES = {
 EXPORTED_SYMBOLS = (
     "attnres_abi_version",
     "attnres_last_error",
+    "attnres_device_status",
     "attnres_lrid_forward",
     "attnres_lrid_backward_workspace_bytes",
     "attnres_lrid_backward",
@@ -59,6 +60,8 @@ def load(path=None):
     L.attnres_abi_version.argtypes = []
     L.attnres_last_error.restype = ctypes.c_char_p
     L.attnres_last_error.argtypes = []
+    L.attnres_device_status.restype = I
+    L.attnres_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint), I]
     L.attnres_lrid_forward.restype = I
     L.attnres_lrid_forward.argtypes = [
         I, I64, I, I, I, I,          # S, N, d, R, H, dtype
@@ -103,6 +106,13 @@ def check(status, what):
     if status != 0:
         msg = load().attnres_last_error().decode(errors="replace")
         raise AttnResError(f"{what} failed ({STATUS_NAMES.get(status, status)}): {msg}")
+
+
+def device_status(reset=False):
+    """Bits set by a bulk-copy kernel that abandoned a bounded wait (0 = healthy)."""
+    st = ctypes.c_uint(0)
+    check(load().attnres_device_status(ctypes.byref(st), int(bool(reset))), "attnres_device_status")
+    return st.value
 
 
 def ptr_array(ptrs):

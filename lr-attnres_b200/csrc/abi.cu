@@ -2,6 +2,7 @@
 // planning, and error reporting. Declared in include/attnres_b200.h.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -80,6 +81,29 @@ bool values_vectorizable(int S, int esz, const void* const* values, const int64_
   return true;
 }
 
+// Which LRID kernel family to use: ATTNRES_B200_PATH=simt forces the
+// register-streaming kernels, =tma requires the bulk-copy pipeline (an error
+// when the layout does not allow it); unset or "auto" picks the pipeline
+// whenever it applies.
+enum PathChoice { PATH_AUTO, PATH_SIMT, PATH_TMA };
+
+PathChoice path_choice() {
+  const char* v = getenv("ATTNRES_B200_PATH");
+  if (!v || !*v || !strcmp(v, "auto")) return PATH_AUTO;
+  if (!strcmp(v, "simt")) return PATH_SIMT;
+  if (!strcmp(v, "tma")) return PATH_TMA;
+  return PATH_AUTO;
+}
+
+// Key rows (and per-token queries) admit 16-byte bulk copies.
+bool keys_bulk_copyable(int S, int R, int esz, const void* const* keys, const int64_t* kstr,
+                        const void* qdyn) {
+  if ((static_cast<long long>(R) * esz) % 16) return false;
+  for (int s = 0; s < S; ++s)
+    if (!aligned16(keys[s]) || (kstr[s] * esz) % 16) return false;
+  return qdyn == nullptr || aligned16(qdyn);
+}
+
 int check_query(int qmode, const void* q, const void* gate, const void* qdyn) {
   switch (qmode) {
     case ATTNRES_QUERY_STATIC:
@@ -111,6 +135,13 @@ int attnres_abi_version(void) { return ATTNRES_ABI_VERSION; }
 
 const char* attnres_last_error(void) { return g_last_error.c_str(); }
 
+int attnres_device_status(unsigned* status, int reset) {
+  if (!status) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "status is NULL");
+  cudaError_t e = attnres::read_device_status(status, reset != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_device_status");
+  return ATTNRES_OK;
+}
+
 int attnres_lrid_forward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
                          int num_heads, int dtype, const void* const* values,
                          const int64_t* value_row_strides, const void* const* keys,
@@ -137,7 +168,16 @@ int attnres_lrid_forward(int num_sources, int64_t num_tokens, int value_dim, int
   attnres::LridIO io{values, value_row_strides, keys, key_row_strides, query_mode, query,
                      query_gate, query_dynamic, logit_scale, key_norm, key_eps, logit_bias,
                      output_norm, output_eps, output, output_inv_rms, alpha_out, key_inv_rms_out};
-  cudaError_t e = attnres::lrid_forward_launch(dtype, plan, io, static_cast<cudaStream_t>(stream));
+  const PathChoice pc = path_choice();
+  attnres::TmaLayout tl{};
+  const bool tma = pc != PATH_SIMT && vec && plan.vec == 16 / esz &&
+                   keys_bulk_copyable(num_sources, key_dim, esz, keys, key_row_strides,
+                                      query_mode != ATTNRES_QUERY_STATIC ? query_dynamic : nullptr) &&
+                   attnres::lrid_tma_layout(plan, esz, false, false, query_mode != ATTNRES_QUERY_STATIC, &tl);
+  if (pc == PATH_TMA && !tma)
+    return fail(ATTNRES_ERR_UNSUPPORTED, "ATTNRES_B200_PATH=tma but the layout does not allow bulk copies");
+  cudaError_t e = tma ? attnres::lrid_tma_forward_launch(dtype, plan, tl, io, static_cast<cudaStream_t>(stream))
+                      : attnres::lrid_forward_launch(dtype, plan, io, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_forward launch");
   return ATTNRES_OK;
 }
@@ -160,6 +200,12 @@ size_t attnres_lrid_backward_workspace_bytes(int num_sources, int64_t num_tokens
     size_t b = 0;
     if (attnres::lrid_workspace(dtype, plan, &b) != cudaSuccess) return 0;
     if (b > best) best = b;
+    for (int variant = 0; variant < 4 && v == 1; ++variant) {
+      attnres::TmaLayout tl{};
+      if (!attnres::lrid_tma_layout(plan, elem_size(dtype), true, variant & 1, variant & 2, &tl)) continue;
+      if (attnres::lrid_tma_workspace(dtype, plan, tl, &b) != cudaSuccess) return 0;
+      if (b > best) best = b;
+    }
   }
   return best;
 }
@@ -205,10 +251,20 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
   rc = attnres::make_lrid_plan(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, vec,
                                output_norm, &plan, &why);
   if (rc) return fail(rc, "%s", why);
+  const PathChoice pc = path_choice();
+  attnres::TmaLayout tl{};
+  const bool tma = pc != PATH_SIMT && vec && plan.vec == 16 / esz &&
+                   keys_bulk_copyable(num_sources, key_dim, esz, keys, key_row_strides,
+                                      query_mode != ATTNRES_QUERY_STATIC ? query_dynamic : nullptr) &&
+                   attnres::lrid_tma_layout(plan, esz, true, output_norm != ATTNRES_NORM_NONE,
+                                            query_mode != ATTNRES_QUERY_STATIC, &tl);
+  if (pc == PATH_TMA && !tma)
+    return fail(ATTNRES_ERR_UNSUPPORTED, "ATTNRES_B200_PATH=tma but the layout does not allow bulk copies");
   const bool need_ws = query_mode != ATTNRES_QUERY_DYNAMIC || grad_logit_bias != nullptr;
   if (need_ws) {
     size_t need = 0;
-    cudaError_t e = attnres::lrid_workspace(dtype, plan, &need);
+    cudaError_t e = tma ? attnres::lrid_tma_workspace(dtype, plan, tl, &need)
+                        : attnres::lrid_workspace(dtype, plan, &need);
     if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward workspace query");
     if (!workspace || workspace_bytes < need)
       return fail(ATTNRES_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
@@ -219,7 +275,8 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
                      output_norm, output_eps, nullptr, nullptr, nullptr, nullptr};
   attnres::LridGradIO gio{grad_output, normed_output, output_inv_rms, grad_values, grad_keys,
                           grad_query, grad_query_gate, grad_query_dynamic, grad_logit_bias, workspace};
-  cudaError_t e = attnres::lrid_backward_launch(dtype, plan, io, gio, static_cast<cudaStream_t>(stream));
+  cudaError_t e = tma ? attnres::lrid_tma_backward_launch(dtype, plan, tl, io, gio, static_cast<cudaStream_t>(stream))
+                      : attnres::lrid_backward_launch(dtype, plan, io, gio, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward launch");
   return ATTNRES_OK;
 }

@@ -23,39 +23,10 @@
 
 #include "common.cuh"
 #include "plan.h"
+#include "lrid_args.cuh"
 
 namespace attnres {
 
-struct LridArgs {
-  LridPlan p;
-  const void* v[kMaxSources];
-  const void* k[kMaxSources];
-  long long vs[kMaxSources];
-  long long ks[kMaxSources];
-  void* gv[kMaxSources];
-  void* gk[kMaxSources];
-  int qmode;
-  const void* q;
-  const void* gate;
-  const void* qdyn;
-  float scale;
-  int key_norm;
-  float key_eps;
-  const float* bias;
-  int out_norm;
-  float out_eps;
-  void* out;
-  float* out_inv;
-  float* alpha_out;
-  float* kinv_out;
-  const void* g;
-  const void* y;
-  const float* y_inv;
-  void* dq_tok;
-  float* partials;
-  int part_stride;
-  int want_bias_grad;
-};
 
 // Sum over the `gsz` consecutive threads of an aligned group (gsz a power of
 // two). Groups wider than a warp combine per-warp sums through `red` in warp

@@ -58,6 +58,15 @@ struct LridGradIO {
   void* workspace;
 };
 
+// Shared-memory pipeline layout of the bulk-copy (TMA) kernels.
+struct TmaLayout {
+  int stages;       // ring depth
+  int stage_bytes;  // bytes per stage: keys [S][tpc][R], values [S][tpc][d], g, y, query
+  int off_v, off_g, off_y, off_qd;  // region offsets inside a stage
+  int stage_off;    // offset of stage 0 from the start of dynamic shared memory
+  int smem_bytes;   // total dynamic shared memory
+};
+
 // Returns 0 and fills *p, or an attnres_status with a message in *why.
 int make_lrid_plan(int S, long long N, int d, int R, int H, int dtype, bool full_vec, int out_norm,
                    LridPlan* p, const char** why);
@@ -65,6 +74,15 @@ cudaError_t lrid_workspace(int dtype, const LridPlan& p, size_t* bytes);
 cudaError_t lrid_forward_launch(int dtype, const LridPlan& p, const LridIO& io, cudaStream_t st);
 cudaError_t lrid_backward_launch(int dtype, const LridPlan& p, const LridIO& io,
                                  const LridGradIO& gio, cudaStream_t st);
+
+// Bulk-copy (TMA) pipelined variant; usable when lrid_tma_layout() succeeds.
+bool lrid_tma_layout(const LridPlan& p, int esz, bool bwd, bool has_y, bool has_qd, TmaLayout* L);
+cudaError_t lrid_tma_workspace(int dtype, const LridPlan& p, const TmaLayout& L, size_t* bytes);
+cudaError_t lrid_tma_forward_launch(int dtype, const LridPlan& p, const TmaLayout& L, const LridIO& io,
+                                    cudaStream_t st);
+cudaError_t lrid_tma_backward_launch(int dtype, const LridPlan& p, const TmaLayout& L, const LridIO& io,
+                                     const LridGradIO& gio, cudaStream_t st);
+cudaError_t read_device_status(unsigned* status, bool reset);
 
 // Base AttnRes read (keys are the rms-normed values): one value row of d
 // columns per token, `tpt` threads per token, `cpt` packs per thread.
