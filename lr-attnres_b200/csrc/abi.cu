@@ -170,13 +170,14 @@ int attnres_lrid_forward(int num_sources, int64_t num_tokens, int value_dim, int
                      output_norm, output_eps, output, output_inv_rms, alpha_out, key_inv_rms_out};
   const PathChoice pc = path_choice();
   attnres::TmaLayout tl{};
+  attnres::LridPlan tplan{};
   const bool tma = pc != PATH_SIMT && vec && plan.vec == 16 / esz &&
                    keys_bulk_copyable(num_sources, key_dim, esz, keys, key_row_strides,
                                       query_mode != ATTNRES_QUERY_STATIC ? query_dynamic : nullptr) &&
-                   attnres::lrid_tma_layout(plan, esz, false, false, query_mode != ATTNRES_QUERY_STATIC, &tl);
+                   attnres::lrid_tma_plan(plan, esz, false, false, query_mode != ATTNRES_QUERY_STATIC, &tplan, &tl);
   if (pc == PATH_TMA && !tma)
     return fail(ATTNRES_ERR_UNSUPPORTED, "ATTNRES_B200_PATH=tma but the layout does not allow bulk copies");
-  cudaError_t e = tma ? attnres::lrid_tma_forward_launch(dtype, plan, tl, io, static_cast<cudaStream_t>(stream))
+  cudaError_t e = tma ? attnres::lrid_tma_forward_launch(dtype, tplan, tl, io, static_cast<cudaStream_t>(stream))
                       : attnres::lrid_forward_launch(dtype, plan, io, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_forward launch");
   return ATTNRES_OK;
@@ -202,8 +203,9 @@ size_t attnres_lrid_backward_workspace_bytes(int num_sources, int64_t num_tokens
     if (b > best) best = b;
     for (int variant = 0; variant < 4 && v == 1; ++variant) {
       attnres::TmaLayout tl{};
-      if (!attnres::lrid_tma_layout(plan, elem_size(dtype), true, variant & 1, variant & 2, &tl)) continue;
-      if (attnres::lrid_tma_workspace(dtype, plan, tl, &b) != cudaSuccess) return 0;
+      attnres::LridPlan tplan{};
+      if (!attnres::lrid_tma_plan(plan, elem_size(dtype), true, variant & 1, variant & 2, &tplan, &tl)) continue;
+      if (attnres::lrid_tma_workspace(dtype, tplan, tl, &b) != cudaSuccess) return 0;
       if (b > best) best = b;
     }
   }
@@ -253,17 +255,18 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
   if (rc) return fail(rc, "%s", why);
   const PathChoice pc = path_choice();
   attnres::TmaLayout tl{};
+  attnres::LridPlan tplan{};
   const bool tma = pc != PATH_SIMT && vec && plan.vec == 16 / esz &&
                    keys_bulk_copyable(num_sources, key_dim, esz, keys, key_row_strides,
                                       query_mode != ATTNRES_QUERY_STATIC ? query_dynamic : nullptr) &&
-                   attnres::lrid_tma_layout(plan, esz, true, output_norm != ATTNRES_NORM_NONE,
-                                            query_mode != ATTNRES_QUERY_STATIC, &tl);
+                   attnres::lrid_tma_plan(plan, esz, true, output_norm != ATTNRES_NORM_NONE,
+                                          query_mode != ATTNRES_QUERY_STATIC, &tplan, &tl);
   if (pc == PATH_TMA && !tma)
     return fail(ATTNRES_ERR_UNSUPPORTED, "ATTNRES_B200_PATH=tma but the layout does not allow bulk copies");
   const bool need_ws = query_mode != ATTNRES_QUERY_DYNAMIC || grad_logit_bias != nullptr;
   if (need_ws) {
     size_t need = 0;
-    cudaError_t e = tma ? attnres::lrid_tma_workspace(dtype, plan, tl, &need)
+    cudaError_t e = tma ? attnres::lrid_tma_workspace(dtype, tplan, tl, &need)
                         : attnres::lrid_workspace(dtype, plan, &need);
     if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward workspace query");
     if (!workspace || workspace_bytes < need)
@@ -275,7 +278,7 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
                      output_norm, output_eps, nullptr, nullptr, nullptr, nullptr};
   attnres::LridGradIO gio{grad_output, normed_output, output_inv_rms, grad_values, grad_keys,
                           grad_query, grad_query_gate, grad_query_dynamic, grad_logit_bias, workspace};
-  cudaError_t e = tma ? attnres::lrid_tma_backward_launch(dtype, plan, tl, io, gio, static_cast<cudaStream_t>(stream))
+  cudaError_t e = tma ? attnres::lrid_tma_backward_launch(dtype, tplan, tl, io, gio, static_cast<cudaStream_t>(stream))
                       : attnres::lrid_backward_launch(dtype, plan, io, gio, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward launch");
   return ATTNRES_OK;

@@ -55,17 +55,25 @@ __device__ __forceinline__ float consumer_group_sum(float v, int gsz, float* red
   return tot;
 }
 
-template <typename T, int KPLMAX, bool BWD>
-__global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ LridArgs a) {
+// Key-segment work of one tile: a segment is one (token slot, source, head)
+// key row slice of dk elements, handled by a group of `key_lanes` lanes that
+// each own `KP * VEC` consecutive elements (16-byte shared loads). All
+// consumer warps share the segments, so the logits of a tile take one or two
+// short rounds instead of a serial loop per token.
+template <typename T, int KP, bool BWD>
+__global__ void __launch_bounds__(288, 2) lrid_tma_kernel(const __grid_constant__ LridArgs a) {
   constexpr int VEC = 16 / sizeof(T);
+  constexpr int KE = KP * VEC;  // key elements per lane
+  constexpr int MAXP = 4;       // (token, key column) pairs per thread in the dq reduction
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const LridPlan& P = a.p;
   const TmaLayout& L = a.tma;
   const int S = P.S, H = P.H, dk = P.dk, dv = P.dv, d = P.d, R = P.R;
-  const int tpt = P.tpt, tpc = P.tpc, tph = P.tph, lph = P.lph, kpl = P.kpl;
+  const int tpt = P.tpt, tpc = P.tpc, tph = P.tph;
   const int nvh = P.nvh, wph = P.wph;
   const int NT = tpc * tpt;
   const int STAGES = L.stages;
+  const int KL = L.key_lanes;
   const bool has_qd = a.qmode != ATTNRES_QUERY_STATIC;
   const bool has_y = BWD && a.out_norm != ATTNRES_NORM_NONE;
 
@@ -79,14 +87,14 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
   T** sgk = sgv + S;
   float* fs = reinterpret_cast<float*>(sgk + S);
   const int A = tpc * H * S;
-  float* sm_logit = fs;
+  float* sm_logit = fs;           // logits, then dlogits (backward)
   float* sm_alpha = fs + A;
   float* sm_kinv = fs + 2 * A;
-  float* sm_qk = fs + 3 * A;
-  float* sm_dwp = fs + 4 * A;
+  float* sm_qk = fs + 3 * A;      // <q, khat>
+  float* sm_dwp = fs + 4 * A;     // backward: per-warp partial <g', v_s>
   float* sm_red = sm_dwp + A * wph;
-  float* sm_dqe = sm_red + (NT >> 5);
-  float* sm_gate = sm_dqe + tpc * R;
+  float* sm_dqc = sm_red + (NT >> 5);        // backward: [tpc][S][R] dq contributions
+  float* sm_dqe = sm_dqc + tpc * S * R;      // [tpc * R] epilogue
   unsigned char* stage0 = smem_raw + L.stage_off;
 
   const int tid = threadIdx.x;
@@ -155,29 +163,33 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
   // ------------------------------------------------------------------------
   const int lane = tid & 31, warp = tid >> 5, nwarps = NT >> 5;
   const int slot = tid / tpt, it = tid % tpt;
-  const int kh = it / lph, kl = it % lph;
-  const bool kvalid = kh < H;
-  const bool kwarp = ((it & ~31) / lph) < H;
   const int vh = it / tph, vj = it % tph;
   const bool vvalid = vh < H && vj < nvh;
   const int hgrp = P.out_norm_group;
   const int width = (a.out_norm == ATTNRES_NORM_ROW) ? d : dv;
   const int col = (vvalid ? vh * dv + vj * VEC : 0);
+  // key-segment mapping (fixed head per thread: the group count is a multiple of H)
+  const int ngroups = NT / KL;
+  const int grp = tid / KL, kl = tid % KL;
+  const int kh = grp % H;
+  const int kcol = kh * dk + kl * KE;        // first key column of this lane
+  const bool klane = kl * KE < dk;
+  const int nseg = tpc * S * H;
+  const int rounds = (nseg + ngroups - 1) / ngroups;
 
-  const T* qp = static_cast<const T*>(a.q);
-  float qs[KPLMAX];
+  float qs[KE];
+  {
+    const T* qp = static_cast<const T*>(a.q);
 #pragma unroll
-  for (int i = 0; i < KPLMAX; ++i) {
-    const int e = kl + i * lph;
-    qs[i] = (a.qmode != ATTNRES_QUERY_DYNAMIC && kvalid && i < kpl && e < dk) ? load_f(qp + kh * dk + e) : 0.f;
+    for (int e = 0; e < KE; ++e)
+      qs[e] = (a.qmode != ATTNRES_QUERY_DYNAMIC && klane) ? load_f(qp + kcol + e) : 0.f;
   }
-  const float gate_h =
-      (a.qmode == ATTNRES_QUERY_GATED && kvalid) ? load_f(static_cast<const T*>(a.gate) + kh) : 0.f;
-  float dq_acc[KPLMAX];
+  const float gate_k = (a.qmode == ATTNRES_QUERY_GATED) ? load_f(static_cast<const T*>(a.gate) + kh) : 0.f;
+  // backward accumulators for the (token slot, key column) pairs this thread reduces
+  float dq_acc[MAXP], dgate_acc[MAXP];
 #pragma unroll
-  for (int i = 0; i < KPLMAX; ++i) dq_acc[i] = 0.f;
-  float dgate_acc = 0.f, dbias_acc = 0.f;
-  float bias_s = 0.f;  // this thread's source bias when it runs the softmax lanes
+  for (int i = 0; i < MAXP; ++i) dq_acc[i] = dgate_acc[i] = 0.f;
+  float dbias_acc = 0.f;
 
   int k = 0;
   for (long long tile = blockIdx.x; tile < P.ntiles; tile += gridDim.x, ++k) {
@@ -195,50 +207,51 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
       break;
     }
     const unsigned char* base = stage0 + static_cast<size_t>(st) * L.stage_bytes;
-    const T* kt = reinterpret_cast<const T*>(base) + slot * R;            // + s*tpc*R
+    const T* kt = reinterpret_cast<const T*>(base);                       // [S][tpc][R]
     const T* vt = reinterpret_cast<const T*>(base + L.off_v) + slot * d;  // + s*tpc*d
+    const T* qdt = reinterpret_cast<const T*>(base + L.off_qd);           // [tpc][R]
 
-    // ---- query for this token -------------------------------------------
-    float q[KPLMAX], qd[KPLMAX];
-    const T* qdt = reinterpret_cast<const T*>(base + L.off_qd) + slot * R + kh * dk;
+    // ---- key phase: key rms-norm and logits, all warps -----------------
+    for (int r = 0; r < rounds; ++r) {
+      const int seg = grp + r * ngroups;
+      const int sl = seg / (S * H);
+      const int s = (seg / H) % S;
+      const bool ok = seg < nseg && tile * tpc + sl < P.N && klane;
+      float ss = 0.f, dot = 0.f;
+      if (ok) {
+        const T* kp = kt + (s * tpc + sl) * R + kcol;
 #pragma unroll
-    for (int i = 0; i < KPLMAX; ++i) {
-      const int e = kl + i * lph;
-      qd[i] = (has_qd && kvalid && tv && i < kpl && e < dk) ? Elem<T>::to_f(qdt[e]) : 0.f;
-      q[i] = (a.qmode == ATTNRES_QUERY_STATIC) ? qs[i]
-             : (a.qmode == ATTNRES_QUERY_DYNAMIC) ? qd[i]
-                                                  : qs[i] + gate_h * qd[i];
-    }
-
-    // ---- key phase --------------------------------------------------------
-    if (kwarp) {
-      for (int s = 0; s < S; ++s) {
-        const T* kp = kt + s * tpc * R + kh * dk;
-        float ss = 0.f, dot = 0.f;
+        for (int pk = 0; pk < KP; ++pk) {
+          const Pack<T, VEC> kr = lds_pack<T, VEC>(kp + pk * VEC);
+          Pack<T, VEC> qr;
+          if (has_qd) qr = lds_pack<T, VEC>(qdt + sl * R + kcol + pk * VEC);
 #pragma unroll
-        for (int i = 0; i < KPLMAX; ++i) {
-          const int e = kl + i * lph;
-          if (i < kpl && kvalid && tv && e < dk) {
-            const float x = Elem<T>::to_f(kp[e]);
+          for (int e = 0; e < VEC; ++e) {
+            const float x = Elem<T>::to_f(kr.e[e]);
+            float qv = qs[pk * VEC + e];
+            if (has_qd) {
+              const float qd = Elem<T>::to_f(qr.e[e]);
+              qv = (a.qmode == ATTNRES_QUERY_DYNAMIC) ? qd : qv + gate_k * qd;
+            }
             ss = fmaf(x, x, ss);
-            dot = fmaf(x, q[i], dot);
+            dot = fmaf(x, qv, dot);
           }
         }
-        ss = group_sum(ss, lph);
-        dot = group_sum(dot, lph);
-        if (kvalid && kl == 0) {
-          const float kinv = a.key_norm ? rsqrtf(ss / dk + a.key_eps) : 1.f;
-          const float qk = dot * kinv;
-          const int idx = (slot * H + kh) * S + s;
-          sm_logit[idx] = qk * a.scale + (a.bias ? a.bias[s] : 0.f);
-          sm_kinv[idx] = kinv;
-          sm_qk[idx] = qk;
-        }
+      }
+      ss = group_sum(ss, KL);
+      dot = group_sum(dot, KL);
+      if (seg < nseg && kl == 0) {
+        const float kinv = a.key_norm ? rsqrtf(ss / dk + a.key_eps) : 1.f;
+        const float qk = dot * kinv;
+        const int idx = (sl * H + kh) * S + s;
+        sm_logit[idx] = qk * a.scale + (a.bias ? a.bias[s] : 0.f);
+        sm_kinv[idx] = kinv;
+        sm_qk[idx] = qk;
       }
     }
     consumer_sync(NT);
 
-    // ---- softmax over sources ---------------------------------------------
+    // ---- softmax over sources: one warp per (token, head) ----------------
     for (int pair = warp; pair < tpc * H; pair += nwarps) {
       const int b = pair * S;
       const long long tp = tile * tpc + pair / H;
@@ -266,7 +279,7 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
     const float* al = sm_alpha + (slot * H + (vh < H ? vh : 0)) * S;
 
     if constexpr (!BWD) {
-      // ---- out = sum_s alpha_s V_s (shared -> registers -> global) -----------
+      // ---- out = sum_s alpha_s V_s (shared -> registers -> global) ---------
       float acc[VEC];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
@@ -290,7 +303,7 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
           for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w, Elem<T>::to_f(r.e[e]), acc[e]);
         }
       }
-      // stage fully read by this warp
+      // this warp is done with the stage
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
       T* outp = static_cast<T*>(a.out);
@@ -313,7 +326,7 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
         }
       }
     } else {
-      // ---- backward: g' (output-norm backward), dV_s = alpha_s g', dw_s ------
+      // ---- backward: g' (output-norm backward), dV_s = alpha_s g', dw_s ----
       const T* gt = reinterpret_cast<const T*>(base + L.off_g) + slot * d;
       float gp[VEC], yv[VEC];
       float gy = 0.f;
@@ -340,7 +353,6 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
         for (int e = 0; e < VEC; ++e) gp[e] = yinv * (gp[e] - yv[e] * mdot);
       }
       const int rg = tph < 32 ? tph : 32;
-      T* dvbase = nullptr;
       for (int s0 = 0; s0 < S; s0 += 4) {
         Pack<T, VEC> r[4];
 #pragma unroll
@@ -359,8 +371,7 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
                 dwp = fmaf(gp[e], Elem<T>::to_f(r[j].e[e]), dwp);
                 gvv[e] = w * gp[e];
               }
-              dvbase = sgv[s];
-              store_pack<T, VEC>(dvbase + t * d + col, gvv);
+              store_pack<T, VEC>(sgv[s] + t * d + col, gvv);
             }
             dwp = group_sum(dwp, rg);
             if ((vj & 31) == 0 && vh < H) sm_dwp[((slot * H + vh) * S + s) * wph + (vj >> 5)] = dwp;
@@ -369,7 +380,7 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
       }
       consumer_sync(NT);
 
-      // ---- dlogit ------------------------------------------------------------
+      // ---- dlogit_s = alpha_s (dw_s - sum_r alpha_r dw_r) -------------------
       for (int pair = warp; pair < tpc * H; pair += nwarps) {
         const int b = pair * S;
         const long long tp = tile * tpc + pair / H;
@@ -388,42 +399,65 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
       if (a.want_bias_grad && tid < S)
         for (int pair = 0; pair < tpc * H; ++pair) dbias_acc += sm_logit[pair * S + tid];
 
-      // ---- key phase 2: dK, dq -------------------------------------------
-      if (kwarp) {
-        float dqt[KPLMAX];
-#pragma unroll
-        for (int i = 0; i < KPLMAX; ++i) dqt[i] = 0.f;
-        for (int s = 0; s < S; ++s) {
-          const int idx = (slot * H + (kvalid ? kh : 0)) * S + s;
+      // ---- key phase 2: dK (global) and dq contributions (shared) -----------
+      for (int r = 0; r < rounds; ++r) {
+        const int seg = grp + r * ngroups;
+        const int sl = seg / (S * H);
+        const int s = (seg / H) % S;
+        const long long ts = tile * tpc + sl;
+        if (seg < nseg && ts < P.N && klane) {
+          const int idx = (sl * H + kh) * S + s;
           const float c1 = sm_logit[idx] * a.scale;
           const float kinv = sm_kinv[idx];
           const float c2 = a.key_norm ? c1 * sm_qk[idx] / dk : 0.f;
-          const T* kp = kt + s * tpc * R + kh * dk;
-          T* gkp = sgk[s] + t * R + kh * dk;
+          const T* kp = kt + (s * tpc + sl) * R + kcol;
+          float* dqc = sm_dqc + (sl * S + s) * R + kcol;
 #pragma unroll
-          for (int i = 0; i < KPLMAX; ++i) {
-            const int e = kl + i * lph;
-            if (i < kpl && kvalid && tv && e < dk) {
-              const float khat = Elem<T>::to_f(kp[e]) * kinv;
-              const float gk = c1 * q[i];
-              gkp[e] = Elem<T>::from_f(a.key_norm ? kinv * (gk - khat * c2) : gk);
-              dqt[i] = fmaf(c1, khat, dqt[i]);
+          for (int pk = 0; pk < KP; ++pk) {
+            const Pack<T, VEC> kr = lds_pack<T, VEC>(kp + pk * VEC);
+            Pack<T, VEC> qr;
+            if (has_qd) qr = lds_pack<T, VEC>(qdt + sl * R + kcol + pk * VEC);
+            float gk[VEC];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+              float qv = qs[pk * VEC + e];
+              if (has_qd) {
+                const float qd = Elem<T>::to_f(qr.e[e]);
+                qv = (a.qmode == ATTNRES_QUERY_DYNAMIC) ? qd : qv + gate_k * qd;
+              }
+              const float khat = Elem<T>::to_f(kr.e[e]) * kinv;
+              const float g0 = c1 * qv;
+              gk[e] = a.key_norm ? kinv * (g0 - khat * c2) : g0;
+              dqc[pk * VEC + e] = c1 * khat;
             }
+            store_pack<T, VEC>(sgk[s] + ts * R + kcol + pk * VEC, gk);
           }
         }
-        T* dqp = static_cast<T*>(a.dq_tok);
+      }
+      consumer_sync(NT);
+
+      // ---- dq: sum the contributions over sources in a fixed order ----------
+      T* dqp = static_cast<T*>(a.dq_tok);
 #pragma unroll
-        for (int i = 0; i < KPLMAX; ++i) {
-          const int e = kl + i * lph;
-          if (i < kpl && kvalid && tv && e < dk) {
+      for (int i = 0; i < MAXP; ++i) {
+        const int pidx = tid + i * NT;
+        if (pidx < tpc * R) {
+          const int sl = pidx / R, e = pidx % R;
+          const long long ts = tile * tpc + sl;
+          if (ts < P.N) {
+            float dq = 0.f;
+            for (int s = 0; s < S; ++s) dq += sm_dqc[(sl * S + s) * R + e];
             if (a.qmode == ATTNRES_QUERY_STATIC) {
-              dq_acc[i] += dqt[i];
+              dq_acc[i] += dq;
             } else if (a.qmode == ATTNRES_QUERY_DYNAMIC) {
-              dqp[t * R + kh * dk + e] = Elem<T>::from_f(dqt[i]);
+              dqp[ts * R + e] = Elem<T>::from_f(dq);
             } else {
-              dqp[t * R + kh * dk + e] = Elem<T>::from_f(gate_h * dqt[i]);
-              dq_acc[i] += dqt[i];
-              dgate_acc = fmaf(dqt[i], qd[i], dgate_acc);
+              const int h = e / dk;
+              const float gte = load_f(static_cast<const T*>(a.gate) + h);
+              const float qd = Elem<T>::to_f(qdt[sl * R + e]);
+              dqp[ts * R + e] = Elem<T>::from_f(gte * dq);
+              dq_acc[i] += dq;
+              dgate_acc[i] = fmaf(dq, qd, dgate_acc[i]);
             }
           }
         }
@@ -433,21 +467,19 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
     }
     consumer_sync(NT);
   }
-  (void)bias_s;
 
   if constexpr (BWD) {
+    // ---- per-CTA partial sums of the parameter gradients, fixed order -------
     if (a.partials == nullptr) return;
-    for (int i = tid; i < tpc * R; i += NT) sm_dqe[i] = 0.f;
-    consumer_sync(NT);
-    if (kvalid) {
+    float* gsm = sm_dqc;  // reuse: [tpc * R] dgate partials
 #pragma unroll
-      for (int i = 0; i < KPLMAX; ++i) {
-        const int e = kl + i * lph;
-        if (i < kpl && e < dk) sm_dqe[slot * R + kh * dk + e] = dq_acc[i];
+    for (int i = 0; i < MAXP; ++i) {
+      const int pidx = tid + i * NT;
+      if (pidx < tpc * R) {
+        sm_dqe[pidx] = dq_acc[i];
+        gsm[pidx] = dgate_acc[i];
       }
     }
-    const float gsum = group_sum(dgate_acc, lph);
-    if (kvalid && kl == 0) sm_gate[slot * H + kh] = gsum;
     consumer_sync(NT);
     float* row = a.partials + static_cast<long long>(blockIdx.x) * a.part_stride;
     for (int e = tid; e < R; e += NT) {
@@ -457,7 +489,8 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
     }
     for (int h = tid; h < H; h += NT) {
       float s = 0.f;
-      for (int sl = 0; sl < tpc; ++sl) s += sm_gate[sl * H + h];
+      for (int sl = 0; sl < tpc; ++sl)
+        for (int e = h * dk; e < (h + 1) * dk; ++e) s += gsm[sl * R + e];
       row[R + h] = s;
     }
     if (tid < S) row[R + H + tid] = dbias_acc;
@@ -470,16 +503,16 @@ __global__ void __launch_bounds__(288) lrid_tma_kernel(const __grid_constant__ L
 using TmaFn = void (*)(LridArgs);
 
 template <typename T>
-static TmaFn pick_tma_t(const LridPlan& p, bool bwd) {
-  if (p.kpl <= 2) return bwd ? lrid_tma_kernel<T, 2, true> : lrid_tma_kernel<T, 2, false>;
-  return bwd ? lrid_tma_kernel<T, 16, true> : lrid_tma_kernel<T, 16, false>;
+static TmaFn pick_tma_t(const TmaLayout& L, bool bwd) {
+  if (L.key_packs == 1) return bwd ? lrid_tma_kernel<T, 1, true> : lrid_tma_kernel<T, 1, false>;
+  return bwd ? lrid_tma_kernel<T, 4, true> : lrid_tma_kernel<T, 4, false>;
 }
 
-static TmaFn pick_tma(int dtype, const LridPlan& p, bool bwd) {
+static TmaFn pick_tma(int dtype, const TmaLayout& L, bool bwd) {
   switch (dtype) {
-    case ATTNRES_DTYPE_F32: return pick_tma_t<float>(p, bwd);
-    case ATTNRES_DTYPE_F16: return pick_tma_t<__half>(p, bwd);
-    default: return pick_tma_t<__nv_bfloat16>(p, bwd);
+    case ATTNRES_DTYPE_F32: return pick_tma_t<float>(L, bwd);
+    case ATTNRES_DTYPE_F16: return pick_tma_t<__half>(L, bwd);
+    default: return pick_tma_t<__nv_bfloat16>(L, bwd);
   }
 }
 
@@ -490,20 +523,43 @@ static int max_smem_optin() {
   return v;
 }
 
-// Shared-memory layout for a plan; false when even two stages do not fit.
-bool lrid_tma_layout(const LridPlan& p, int esz, bool bwd, bool has_y, bool has_qd, TmaLayout* L) {
-  if (p.tpt * p.tpc > 256 || p.cph != 1) return false;
-  const int tpc = p.tpc;
+static int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
+}
+
+static bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
+
+// Pipeline plan for the bulk-copy kernels: token rows per tile, key-lane
+// mapping and the shared-memory ring. False when the geometry is outside what
+// these kernels handle (the caller then uses the register-streaming kernels).
+bool lrid_tma_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool has_qd, LridPlan* out,
+                   TmaLayout* L) {
+  const int VEC = 16 / esz;
+  if (base.vec != VEC || base.cph != 1 || base.tpt > 256) return false;
+  if (!is_pow2(base.H) || base.dk % VEC) return false;
+  const int kp = (base.dk <= 32 * VEC) ? 1 : 4;
+  const int ke = kp * VEC;
+  if (base.dk % ke) return false;
+  const int kl = base.dk / ke;
+  if (!is_pow2(kl) || kl > 32) return false;
+  LridPlan p = base;
+  int tpc = 256 / p.tpt;
+  const int want = env_int("ATTNRES_TMA_TPC", 0);
+  if (want > 0 && want <= tpc && is_pow2(want)) tpc = want;
+  p.tpc = tpc;
+  p.ntiles = (p.N + tpc - 1) / tpc;
+  const int NT = tpc * p.tpt;
+  if ((NT / kl) % p.H) return false;
+  if (tpc * p.R > 4 * NT) return false;
   size_t off = 0;
   off += 2 * kMaxStages * sizeof(uint64_t);
   off += 6 * sizeof(void*) * p.S;
   const size_t A = static_cast<size_t>(tpc) * p.H * p.S;
-  off += sizeof(float) * (4 * A + A * p.wph + (p.tpc * p.tpt) / 32 + static_cast<size_t>(tpc) * p.R +
-                          static_cast<size_t>(tpc) * p.H);
+  off += sizeof(float) * (4 * A + A * p.wph + NT / 32);
+  if (bwd) off += sizeof(float) * (static_cast<size_t>(tpc) * p.S * p.R + static_cast<size_t>(tpc) * p.R);
   off = (off + 127) & ~static_cast<size_t>(127);
-  size_t sb = 0;
-  const size_t kbytes = static_cast<size_t>(p.S) * tpc * p.R * esz;
-  sb += kbytes;
+  size_t sb = static_cast<size_t>(p.S) * tpc * p.R * esz;
   const int off_v = static_cast<int>(sb);
   sb += static_cast<size_t>(p.S) * tpc * p.d * esz;
   const int off_g = static_cast<int>(sb);
@@ -515,12 +571,21 @@ bool lrid_tma_layout(const LridPlan& p, int esz, bool bwd, bool has_y, bool has_
   sb = (sb + 127) & ~static_cast<size_t>(127);
   const size_t cap = static_cast<size_t>(max_smem_optin());
   if (cap == 0 || off + 2 * sb > cap) return false;
-  // Two CTAs per SM when two stages each fit in half of the SM's shared
-  // memory; otherwise one CTA with as deep a ring as fits.
-  const size_t half = (cap + 1024) / 2 - 1024;
-  size_t budget = (off + 2 * sb <= half) ? half : cap;
+  // Shared memory is split between `ctas` co-resident CTAs per SM (each keeps
+  // at least two stages); each CTA takes as deep a ring as its share allows.
+  int ctas = env_int("ATTNRES_TMA_CTAS", 2);
+  if (ctas < 1) ctas = 1;
+  size_t budget = cap;
+  for (; ctas > 1; --ctas) {
+    const size_t share = (cap + 1024) / ctas - 1024;
+    if (off + 2 * sb <= share) {
+      budget = share;
+      break;
+    }
+  }
   int stages = static_cast<int>((budget - off) / sb);
-  stages = std::min(stages, kMaxStages);
+  stages = std::min(stages, std::min(kMaxStages, env_int("ATTNRES_TMA_MAX_STAGES", kMaxStages)));
+  if (stages < 2) stages = 2;
   L->stages = stages;
   L->stage_bytes = static_cast<int>(sb);
   L->off_v = off_v;
@@ -529,6 +594,9 @@ bool lrid_tma_layout(const LridPlan& p, int esz, bool bwd, bool has_y, bool has_
   L->off_qd = off_qd;
   L->stage_off = static_cast<int>(off);
   L->smem_bytes = static_cast<int>(off + stages * sb);
+  L->key_lanes = kl;
+  L->key_packs = kp;
+  *out = p;
   return true;
 }
 
@@ -538,7 +606,7 @@ struct TmaShape {
 };
 
 static cudaError_t tma_shape(int dtype, const LridPlan& p, const TmaLayout& L, bool bwd, TmaShape* ts) {
-  ts->fn = pick_tma(dtype, p, bwd);
+  ts->fn = pick_tma(dtype, L, bwd);
   ts->block = p.tpc * p.tpt + 32;
   cudaError_t e = cudaFuncSetAttribute(ts->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_bytes);
   if (e != cudaSuccess) return e;

@@ -65,6 +65,8 @@ struct TmaLayout {
   int off_v, off_g, off_y, off_qd;  // region offsets inside a stage
   int stage_off;    // offset of stage 0 from the start of dynamic shared memory
   int smem_bytes;   // total dynamic shared memory
+  int key_lanes;    // lanes per key segment (power of two <= 32)
+  int key_packs;    // 16-byte packs per key lane (1 or 4)
 };
 
 // Returns 0 and fills *p, or an attnres_status with a message in *why.
@@ -76,7 +78,8 @@ cudaError_t lrid_backward_launch(int dtype, const LridPlan& p, const LridIO& io,
                                  const LridGradIO& gio, cudaStream_t st);
 
 // Bulk-copy (TMA) pipelined variant; usable when lrid_tma_layout() succeeds.
-bool lrid_tma_layout(const LridPlan& p, int esz, bool bwd, bool has_y, bool has_qd, TmaLayout* L);
+bool lrid_tma_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool has_qd, LridPlan* out,
+                   TmaLayout* L);
 cudaError_t lrid_tma_workspace(int dtype, const LridPlan& p, const TmaLayout& L, size_t* bytes);
 cudaError_t lrid_tma_forward_launch(int dtype, const LridPlan& p, const TmaLayout& L, const LridIO& io,
                                     cudaStream_t st);
