@@ -87,6 +87,16 @@ cudaError_t lrid_tma_backward_launch(int dtype, const LridPlan& p, const TmaLayo
                                      const LridGradIO& gio, cudaStream_t st);
 cudaError_t read_device_status(unsigned* status, bool reset);
 
+// Warp-per-token bulk-copy variant (row widths that split into 32-lane chunks per head).
+bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool has_qd, int out_norm,
+                    TmaLayout* L, int* consumer_warps);
+cudaError_t lrid_warp_workspace(int dtype, const LridPlan& p, const TmaLayout& L, int nw, size_t* bytes);
+cudaError_t lrid_warp_forward_launch(int dtype, const LridPlan& p, const TmaLayout& L, int nw,
+                                     const LridIO& io, cudaStream_t st);
+cudaError_t lrid_warp_backward_launch(int dtype, const LridPlan& p, const TmaLayout& L, int nw,
+                                      const LridIO& io, const LridGradIO& gio, cudaStream_t st);
+cudaError_t read_warp_status(unsigned* status, bool reset);
+
 // Base AttnRes read (keys are the rms-normed values): one value row of d
 // columns per token, `tpt` threads per token, `cpt` packs per thread.
 struct BasePlan {

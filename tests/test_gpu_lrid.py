@@ -15,14 +15,15 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["auto", "simt"])
+@pytest.fixture(autouse=True, params=["auto", "tma", "simt"])
 def kernel_path(request, monkeypatch):
-    """Run every LRID test on both kernel families: the bulk-copy (TMA)
-    pipeline that `auto` picks for aligned layouts, and the register-streaming
-    kernels (`simt`) that serve every other layout."""
+    """Run every LRID test on each kernel family: `auto` picks the
+    warp-per-token bulk-copy pipeline where the row widths allow it, `tma` the
+    CTA-tile bulk-copy pipeline, `simt` the register-streaming kernels that
+    serve every layout (each falls back to the next when its rules fail)."""
     monkeypatch.setenv("ATTNRES_B200_PATH", request.param)
     yield request.param
-    if request.param == "auto":
+    if request.param != "simt":
         from attnres_b200 import _native
 
         assert _native.device_status(reset=True) == 0, "a pipeline kernel abandoned a bounded wait"
