@@ -543,6 +543,10 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
   if (off + 2 * sb > static_cast<size_t>(cap)) return false;
   int stages = static_cast<int>((cap - off) / sb);
   stages = std::min(stages, std::min(kWarpMaxStages, env_int_w("ATTNRES_WARP_MAX_STAGES", kWarpMaxStages)));
+  // A consumer warp may only wait on a stage whose previous occupant has been
+  // filled, or the mbarrier parity would alias two phases: never more
+  // consumer warps than stages.
+  nw = std::min(nw, stages);
   L->stages = stages;
   L->stage_bytes = static_cast<int>(sb);
   L->off_v = off_v;

@@ -173,6 +173,17 @@ def test_lrid_shapes_bf16(name, S, D, R, H, scale, query_kind, norm):
     compare(res, ref, torch.bfloat16, B * T)
 
 
+def test_lrid_config3_many_tokens_per_cta():
+    """BASELINE config-3 row shape with enough tokens that every persistent CTA
+    walks its stage ring several times (single-token stages of 57 KB leave
+    only a few stages, fewer than the consumer warps a CTA could run)."""
+    S, B, T, D, R, H = 13, 1, 1500, 2048, 64, 4
+    inp = make_inputs(S, B * T, D, R, H, seed=77, query_std=0.02)
+    res = run_lrid(inp, B, T, H, 0.25, True, "gated", torch.bfloat16)
+    ref = oracle_lrid(inp, H, 0.25, True, "gated", torch.bfloat16, oracle.NORM_NONE, False)
+    compare(res, ref, torch.bfloat16, B * T)
+
+
 def test_lrid_strided_and_misaligned_sources():
     """Keys as a column slice of a wider row (output-tail keys,
     tests/test_attnres_ops.py:934-972) and values offset by one element, which
