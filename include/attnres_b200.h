@@ -148,6 +148,37 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
                           size_t workspace_bytes, void* stream);
 
 /*
+ * LRID read backward that allocates nothing: for callers that cannot call
+ * cudaMalloc or hand over a device workspace (a custom allocator's own
+ * callbacks, plugins that receive only fixed buffers, runtimes that reserve
+ * all device memory up front). Same arguments and results as
+ * attnres_lrid_backward minus the workspace: the scratch for the parameter
+ * gradients' partial sums is a static device array of
+ * attnres_noalloc_scratch_bytes() bytes (4 MiB) that every GPU loading the
+ * library holds until the process exits. Geometries needing more scratch are
+ * rejected with ATTNRES_ERR_UNSUPPORTED. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture. All calls share the one array: calls that
+ * overlap on the GPU (other streams, other threads) race on it.
+ * No counterpart in the reference.
+ */
+int attnres_lrid_backward_noalloc(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                  int num_heads, int dtype,
+                                  const void* const* values, const int64_t* value_row_strides,
+                                  const void* const* keys, const int64_t* key_row_strides,
+                                  int query_mode, const void* query, const void* query_gate,
+                                  const void* query_dynamic, float logit_scale, int key_norm,
+                                  float key_eps, const float* logit_bias, int output_norm,
+                                  float output_eps, const void* grad_output,
+                                  const void* normed_output, const float* output_inv_rms,
+                                  void* const* grad_values, void* const* grad_keys,
+                                  void* grad_query, float* grad_query_gate,
+                                  void* grad_query_dynamic, float* grad_logit_bias, void* stream);
+
+/* Size in bytes of the static scratch used by attnres_lrid_backward_noalloc. */
+size_t attnres_noalloc_scratch_bytes(void);
+
+/*
  * Base AttnRes read, forward (keys are the values themselves).
  * Replaces _attnres_read_list_triton (attnres_ops.py:2301) /
  * _attnres_list_read_kernel (attnres_ops.py:267).

@@ -32,6 +32,8 @@ EXPORTED_SYMBOLS = (
     "attnres_base_forward",
     "attnres_base_backward_workspace_bytes",
     "attnres_base_backward",
+    "attnres_lrid_backward_noalloc",
+    "attnres_noalloc_scratch_bytes",
 )
 
 _lib = None
@@ -87,6 +89,10 @@ def load(path=None):
         P, SZ,                       # workspace, bytes
         P,                           # stream
     ]
+    L.attnres_lrid_backward_noalloc.restype = I
+    L.attnres_lrid_backward_noalloc.argtypes = L.attnres_lrid_backward.argtypes[:-3] + [P]
+    L.attnres_noalloc_scratch_bytes.restype = SZ
+    L.attnres_noalloc_scratch_bytes.argtypes = []
     L.attnres_base_forward.restype = I
     L.attnres_base_forward.argtypes = [
         I, I64, I, I, PP, PI64, P, I, F, P, I, F, P, P, P,

@@ -133,6 +133,8 @@ int check_norm(int mode, bool allow_per_head) {
 
 }  // namespace
 
+int attnres::record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 int attnres_abi_version(void) { return ATTNRES_ABI_VERSION; }

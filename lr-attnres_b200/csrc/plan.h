@@ -140,3 +140,8 @@ namespace attnres {
 void launch_reduce_partials(const float* partials, int nrows, int stride, int c0, int ncols,
                             float* out, cudaStream_t st);
 }  // namespace attnres
+
+namespace attnres {
+// Records `msg` as attnres_last_error() for the calling host thread; returns code.
+int record_error(int code, const char* msg);
+}  // namespace attnres
