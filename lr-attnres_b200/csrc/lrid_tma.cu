@@ -202,10 +202,16 @@ __global__ void __launch_bounds__(288, 2) lrid_tma_kernel(const __grid_constant_
       yinv = (a.out_norm == ATTNRES_NORM_PER_HEAD) ? a.y_inv[t * H + vh] : a.y_inv[t];
 
     const bool landed = mbar_wait_bounded(&full[st], par);
-    if (consumer_sync_or(NT, !landed)) {
-      if (tid == 0) atomicOr(&g_device_status, kStatusFullWaitTimeout);
-      break;
+    if constexpr (BWD) {
+      if (consumer_sync_or(NT, !landed)) {
+        if (tid == 0) atomicOr(&g_device_status, kStatusFullWaitTimeout);
+        break;
+      }
     }
+    // forward: logits / key inv-rms double-buffered by tile parity, so the
+    // key-phase barrier is the only CTA barrier of a tile
+    float* lg_t = BWD ? sm_logit : sm_logit + (k & 1) * A;
+    float* ki_t = BWD ? sm_kinv : fs + 2 * A + (k & 1) * A;
     const unsigned char* base = stage0 + static_cast<size_t>(st) * L.stage_bytes;
     const T* kt = reinterpret_cast<const T*>(base);                       // [S][tpc][R]
     const T* vt = reinterpret_cast<const T*>(base + L.off_v) + slot * d;  // + s*tpc*d
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(288, 2) lrid_tma_kernel(const __grid_constant_
       const int seg = grp + r * ngroups;
       const int sl = seg / (S * H);
       const int s = (seg / H) % S;
-      const bool ok = seg < nseg && tile * tpc + sl < P.N && klane;
+      const bool ok = landed && seg < nseg && tile * tpc + sl < P.N && klane;
       float ss = 0.f, dot = 0.f;
       if (ok) {
         const T* kp = kt + (s * tpc + sl) * R + kcol;
@@ -244,14 +250,54 @@ __global__ void __launch_bounds__(288, 2) lrid_tma_kernel(const __grid_constant_
         const float kinv = a.key_norm ? rsqrtf(ss / dk + a.key_eps) : 1.f;
         const float qk = dot * kinv;
         const int idx = (sl * H + kh) * S + s;
-        sm_logit[idx] = qk * a.scale + (a.bias ? a.bias[s] : 0.f);
-        sm_kinv[idx] = kinv;
-        sm_qk[idx] = qk;
+        lg_t[idx] = qk * a.scale + (a.bias ? a.bias[s] : 0.f);
+        ki_t[idx] = kinv;
+        if (BWD) sm_qk[idx] = qk;
       }
     }
-    consumer_sync(NT);
+    if constexpr (BWD) {
+      consumer_sync(NT);
+    } else {
+      if (consumer_sync_or(NT, !landed)) {
+        if (tid == 0) atomicOr(&g_device_status, kStatusFullWaitTimeout);
+        break;
+      }
+    }
 
-    // ---- softmax over sources: one warp per (token, head) ----------------
+    // ---- softmax over sources ---------------------------------------------
+    // forward: every warp computes the softmax of its own token into private
+    // scratch (no barrier); backward: one warp per (token, head), shared.
+    const float* al;
+    if constexpr (!BWD) {
+      float* wal = sm_red + (NT >> 5) + warp * H * S;  // after the reduction slots
+      const int ws = (warp * 32) / tpt;  // token slot of this warp
+      const long long tw = tile * tpc + ws;
+      // heads read by this warp's value threads (one head when tph >= 32)
+      const int it0 = (warp * 32) % tpt;
+      const int h_lo = it0 / tph;
+      const int h_hi = min(H - 1, (it0 + 31) / tph);
+      for (int h = h_lo; h <= h_hi; ++h) {
+        const bool writer = h * tph >= it0 && h * tph < it0 + 32;  // warp holding the head's first thread
+        const float* lg = lg_t + (ws * H + h) * S;
+        const float l0 = lane < S ? lg[lane] : -INFINITY;
+        const float l1 = lane + 32 < S ? lg[lane + 32] : -INFINITY;
+        const float m = warp_max(fmaxf(l0, l1));
+        const float e0 = lane < S ? expf(l0 - m) : 0.f;
+        const float e1 = lane + 32 < S ? expf(l1 - m) : 0.f;
+        const float sum = warp_sum(e0 + e1);
+        if (lane < S) wal[h * S + lane] = e0 / sum;
+        if (lane + 32 < S) wal[h * S + lane + 32] = e1 / sum;
+        if (writer && tw < P.N) {
+          const float* kv = ki_t + (ws * H + h) * S;
+          for (int s = lane; s < S; s += 32) {
+            if (a.alpha_out) a.alpha_out[(tw * H + h) * S + s] = s < 32 ? e0 / sum : e1 / sum;
+            if (a.kinv_out) a.kinv_out[(tw * H + h) * S + s] = kv[s];
+          }
+        }
+      }
+      __syncwarp();
+      al = wal + (vh < H ? vh : 0) * S;
+    } else {
     for (int pair = warp; pair < tpc * H; pair += nwarps) {
       const int b = pair * S;
       const long long tp = tile * tpc + pair / H;
@@ -276,7 +322,8 @@ __global__ void __launch_bounds__(288, 2) lrid_tma_kernel(const __grid_constant_
       }
     }
     consumer_sync(NT);
-    const float* al = sm_alpha + (slot * H + (vh < H ? vh : 0)) * S;
+    al = sm_alpha + (slot * H + (vh < H ? vh : 0)) * S;
+    }
 
     if constexpr (!BWD) {
       // ---- out = sum_s alpha_s V_s (shared -> registers -> global) ---------
@@ -464,8 +511,8 @@ __global__ void __launch_bounds__(288, 2) lrid_tma_kernel(const __grid_constant_
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
+      consumer_sync(NT);
     }
-    consumer_sync(NT);
   }
 
   if constexpr (BWD) {
@@ -558,6 +605,7 @@ bool lrid_tma_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool has
   const size_t A = static_cast<size_t>(tpc) * p.H * p.S;
   off += sizeof(float) * (4 * A + A * p.wph + NT / 32);
   if (bwd) off += sizeof(float) * (static_cast<size_t>(tpc) * p.S * p.R + static_cast<size_t>(tpc) * p.R);
+  else off += sizeof(float) * (static_cast<size_t>(NT / 32) * p.H * p.S);  // per-warp softmax
   off = (off + 127) & ~static_cast<size_t>(127);
   size_t sb = static_cast<size_t>(p.S) * tpc * p.R * esz;
   const int off_v = static_cast<int>(sb);

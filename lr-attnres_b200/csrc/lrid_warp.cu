@@ -29,7 +29,7 @@ namespace attnres {
 
 static __device__ unsigned int g_warp_status = 0;
 
-constexpr int kStreamMaxWarps = 16;
+constexpr int kStreamMaxWarps = 20;
 constexpr int kStreamMaxStages = 4;
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -37,7 +37,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 template <typename T, int KP, int SMAX, bool BWD>
-__global__ void __launch_bounds__(512, 1) lrid_stream_kernel(const __grid_constant__ LridArgs a) {
+__global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const __grid_constant__ LridArgs a) {
   constexpr int VEC = 16 / sizeof(T);
   constexpr int KE = KP * VEC;
   constexpr int CW = 32 * VEC;  // columns per chunk unit (512 bytes per row)
@@ -486,8 +486,8 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
   const size_t sb = align_up(std::max(key_unit, chunk_unit), 128);
   const size_t kcopy_off = align_up(5 * SH * sizeof(float), 16);
   const size_t wscr = align_up(kcopy_off + (bwd ? key_unit : 0), 128);
-  const int nsw = std::max(2, std::min(kStreamMaxStages, env_int_w("ATTNRES_STREAM_STAGES", bwd ? 2 : 3)));
-  const int max_warps = 16;
+  const int nsw = std::max(2, std::min(kStreamMaxStages, env_int_w("ATTNRES_STREAM_STAGES", 2)));
+  const int max_warps = bwd ? 16 : 20;
   int nw = std::min(max_warps, std::max(1, env_int_w("ATTNRES_STREAM_WARPS", max_warps)));
   for (; nw >= 1; --nw) {
     size_t off = kStreamMaxWarps * kStreamMaxStages * sizeof(uint64_t) + 6 * sizeof(void*) * base.S;
