@@ -188,6 +188,20 @@ def run_reference(args, c):
     print(json.dumps(line), flush=True)
 
 
+def profiled_traffic_per_token():
+    """DRAM bytes per token of each kernel, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "lrid_kernels_config2_small.md")
+    out = {}
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_token:"):
+                _, kernel, value = [x.strip() for x in line.split(":")]
+                out[kernel] = float(value)
+    except OSError:
+        pass
+    return out
+
+
 def config_block(c, args):
     return {
         "workload": f"{args.config}: LRID read fwd+bwd, S={c['S']}, N={c['B']}x{c['T']} tokens per GPU, "
@@ -333,6 +347,7 @@ def main():
     except Exception:
         pass
     hbm = float(peaks.get("hbm_gbs", 6650.0))
+    traffic = profiled_traffic_per_token()
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     bwd_gbs = tokens * bwd_b / (bwd_ms * 1e-3) / 1e9
     fwd_gbs = tokens * fwd_b / (fwd_ms * 1e-3) / 1e9
@@ -357,10 +372,11 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) values/keys/grads, query N(0,0.02))",
             "config": config_block(c, args),
             "roofline": {
-                "kernel": "lrid_kernel<bf16,8,1,2,bwd> (backward)", "bound": "hbm",
+                "kernel": "backward LRID read (lrid_stream_kernel for this row shape)", "bound": "hbm",
                 "achieved": bwd_gbs, "peak": hbm, "unit": "GB/s", "frac": bwd_gbs / hbm,
                 "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs" if peak_src == "measured" else "fallback 6650 GB/s",
-                "traffic": None,
+                "traffic": (traffic.get("backward", 0) * tokens) if (traffic and args.config == "config2") else None,
+                "traffic_source": "ncu dram read+write per token x tokens, profiles/lrid_kernels_config2_small.md",
                 "algorithmic_bytes_per_token": bwd_b, "kernel_ms": bwd_ms,
                 "forward": {"achieved": fwd_gbs, "frac": fwd_gbs / hbm, "kernel_ms": fwd_ms,
                             "algorithmic_bytes_per_token": fwd_b},
