@@ -265,11 +265,12 @@ def main():
         return ops.lrid_read_backward(x["values"], x["keys"], q, gate, qdyn, None, x["grad"], out, inv,
                                       H, scale, True, 0)
 
+    from attnres_b200.sharding import allreduce_param_grads
+
     def allreduce(dq, dgate):
+        # the only cross-GPU step: one bucketed NCCL all-reduce of the summed grads
         if world > 1:
-            dist.all_reduce(dq)
-            if gated:
-                dist.all_reduce(dgate)
+            allreduce_param_grads([dq, dgate] if gated else [dq])
 
     stream = torch.cuda.Stream(device)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
