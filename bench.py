@@ -301,11 +301,41 @@ def main():
 
     sampler = ClockSampler(local)
     sampler.start()
+    # The gradient all-reduce of step k runs on its own stream, overlapping the
+    # forward of step k+1 (which does not read it); the backward of step k+1,
+    # which rewrites the gradient buffers, waits for it.
+    comm = torch.cuda.Stream(device)
+    bwd_done = [torch.cuda.Event() for _ in range(2)]
+    comm_done = [torch.cuda.Event() for _ in range(2)]
+
+    def step(i, fe=None, be=None):
+        if fe:
+            fe[0].record(stream)
+        g_fwd.replay()
+        if fe:
+            fe[1].record(stream)
+        if world > 1 and i > 0:
+            stream.wait_event(comm_done[(i - 1) % 2])
+        if be:
+            be[0].record(stream)
+        g_bwd.replay()
+        if be:
+            be[1].record(stream)
+        if world > 1:
+            bwd_done[i % 2].record(stream)
+            comm.wait_event(bwd_done[i % 2])
+            with torch.cuda.stream(comm):
+                allreduce(dq, dgate)
+                comm_done[i % 2].record(comm)
+
+    def drain(last):
+        if world > 1:
+            stream.wait_event(comm_done[last % 2])
+
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            g_fwd.replay()
-            g_bwd.replay()
-            allreduce(dq, dgate)
+        for i in range(args.warmup):
+            step(i)
+        drain(args.warmup - 1)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -318,13 +348,8 @@ def main():
     with torch.cuda.stream(stream):
         ev[0].record(stream)
         for i in range(args.steps):
-            fwd_events[i][0].record(stream)
-            g_fwd.replay()
-            fwd_events[i][1].record(stream)
-            bwd_events[i][0].record(stream)
-            g_bwd.replay()
-            bwd_events[i][1].record(stream)
-            allreduce(dq, dgate)
+            step(i, fwd_events[i], bwd_events[i])
+        drain(args.steps - 1)
         ev[1].record(stream)
     torch.cuda.synchronize()
     if world > 1:
