@@ -179,6 +179,37 @@ int attnres_lrid_backward_noalloc(int num_sources, int64_t num_tokens, int value
 size_t attnres_noalloc_scratch_bytes(void);
 
 /*
+ * Key-from-value projection of the LRID read (lrid_key_from_value, unshared):
+ *   keys[s][n][:] = inv_rms[s][n] * (V_s[n] @ W^T),
+ *   inv_rms = value_norm ? rsqrt(mean(V_s[n]^2) + value_eps) : 1
+ * i.e. rms_norm(V_s) @ value_key_proj.weight^T. Replaces
+ * LRIDFusedProjection.project_key_from_value (model.py:348-356) and the value
+ * norm of model.py:344-346. weight: dtype [R, d] (row stride weight_row_stride).
+ * keys: dtype [S][N][R] dense; inv_rms: float [S][N] (needed by the backward).
+ * bf16/fp16 with d % 64 == 0, R % 16 == 0 (16..256) and 16-byte aligned rows
+ * run on tcgen05 tensor cores (TMA-fed, accumulators in TMEM); any other
+ * layout on CUDA cores.
+ */
+int attnres_lrid_key_projection(int num_sources, int64_t num_tokens, int value_dim, int key_dim, int dtype,
+                                const void* const* values, const int64_t* value_row_strides,
+                                const void* weight, int64_t weight_row_stride, int value_norm,
+                                float value_eps, void* keys, float* inv_rms, void* stream);
+
+/*
+ * Backward of the value rms-norm in the key projection, accumulated into
+ * grad_values (dense [N, d] each):
+ *   grad_values[s][n] += inv * (dn - (V*inv) * <dK, key> / d)
+ * grad_normed = dK @ W: dtype [S][N][d]; grad_keys = dK: dtype [S][N][R];
+ * keys / inv_rms: the forward's outputs. (The weight gradient
+ * sum_s (inv_s * dK_s)^T @ V_s is a plain GEMM left to the caller.)
+ */
+int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                         int dtype, const void* const* values,
+                                         const int64_t* value_row_strides, void* const* grad_values,
+                                         const void* grad_normed, const void* grad_keys, const void* keys,
+                                         const float* inv_rms, int value_norm, void* stream);
+
+/*
  * Base AttnRes read, forward (keys are the values themselves).
  * Replaces _attnres_read_list_triton (attnres_ops.py:2301) /
  * _attnres_list_read_kernel (attnres_ops.py:267).

@@ -13,6 +13,8 @@ from .ops import (
     is_fused_attnres_available,
     lrid_attention_residual_read,
     lrid_attention_residual_read_gated,
+    lrid_attention_residual_read_key_from_value,
+    lrid_kv_read,
     lrid_read,
     lrid_read_list,
     lrid_read_list_backward,
@@ -25,6 +27,8 @@ __all__ = [
     "is_fused_attnres_available",
     "lrid_attention_residual_read",
     "lrid_attention_residual_read_gated",
+    "lrid_attention_residual_read_key_from_value",
+    "lrid_kv_read",
     "lrid_read",
     "lrid_read_list",
     "lrid_read_list_backward",

@@ -33,6 +33,8 @@ EXPORTED_SYMBOLS = (
     "attnres_base_backward_workspace_bytes",
     "attnres_base_backward",
     "attnres_lrid_backward_noalloc",
+    "attnres_lrid_key_projection",
+    "attnres_lrid_key_projection_backward",
     "attnres_noalloc_scratch_bytes",
 )
 
@@ -93,6 +95,10 @@ def load(path=None):
     L.attnres_lrid_backward_noalloc.argtypes = L.attnres_lrid_backward.argtypes[:-3] + [P]
     L.attnres_noalloc_scratch_bytes.restype = SZ
     L.attnres_noalloc_scratch_bytes.argtypes = []
+    L.attnres_lrid_key_projection.restype = I
+    L.attnres_lrid_key_projection.argtypes = [I, I64, I, I, I, PP, PI64, P, I64, I, F, P, P, P]
+    L.attnres_lrid_key_projection_backward.restype = I
+    L.attnres_lrid_key_projection_backward.argtypes = [I, I64, I, I, I, PP, PI64, PP, P, P, P, P, I, P]
     L.attnres_base_forward.restype = I
     L.attnres_base_forward.argtypes = [
         I, I64, I, I, PP, PI64, P, I, F, P, I, F, P, P, P,

@@ -698,3 +698,207 @@ def is_fused_attnres_available() -> bool:
     except N.AttnResError:
         return False
     return torch.cuda.is_available()
+
+
+# ---------------------------------------------------------------------------
+# attnres::lrid_kv_read — LRID read with keys projected from the values
+# (lrid_key_from_value: keys_s = rms_norm(V_s) @ W^T, model.py:344-356)
+# ---------------------------------------------------------------------------
+def _kv_project(values, weight, value_norm):
+    S = len(values)
+    d = values[0].size(-1)
+    R = weight.size(0)
+    if weight.dim() != 2 or weight.size(1) != d:
+        raise RuntimeError(f"attnres_b200: key weight must be [R, {d}] (nn.Linear weight)")
+    dtype = values[0].dtype
+    _require_cuda([*values, weight], "key projection inputs")
+    rows, strides = _sources(values, d, dtype)
+    n = _ntok(values[0])
+    device = values[0].device
+    w = weight.to(dtype)
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    keys = torch.empty((S, *_lead_shape(values[0]), R), device=device, dtype=dtype)
+    inv = torch.empty((S, n), device=device, dtype=torch.float32)
+    with torch.cuda.device(device):
+        rc = N.load().attnres_lrid_key_projection(
+            S, n, d, R, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            _ptr(w), int(w.stride(0)), int(bool(value_norm)), float(torch.finfo(dtype).eps),
+            _ptr(keys), _ptr(inv), _stream_ptr(device))
+    N.check(rc, "attnres_lrid_key_projection")
+    return keys, inv
+
+
+@torch.library.custom_op("attnres::lrid_kv_read", mutates_args=())
+def lrid_kv_read(
+    values: List[Tensor],
+    key_weight: Tensor,
+    query: Optional[Tensor],
+    query_gate: Optional[Tensor],
+    query_dynamic: Optional[Tensor],
+    logit_bias: Optional[Tensor],
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    output_norm: int,
+    value_norm: bool,
+) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Returns (out, output_inv_rms, keys [S, *lead, R], value_inv_rms [S, N])."""
+    values = list(values)
+    keys, inv = _kv_project(values, key_weight, value_norm)
+    out, oinv, _, _ = _lrid_forward_impl(values, list(keys.unbind(0)), query, query_gate, query_dynamic,
+                                         logit_bias, num_heads, logit_scale, key_norm, int(output_norm), False)
+    return out, oinv, keys, inv
+
+
+@lrid_kv_read.register_fake
+def _(values, key_weight, query, query_gate, query_dynamic, logit_bias, num_heads, logit_scale, key_norm,
+      output_norm, value_norm):
+    v0 = values[0]
+    n = v0.numel() // v0.size(-1)
+    S, R = len(values), key_weight.size(0)
+    shape = {N.NORM_PER_HEAD: (n, int(num_heads)), N.NORM_ROW: (n,)}.get(int(output_norm), (1,))
+    return (v0.new_empty(v0.shape), v0.new_empty(shape, dtype=torch.float32),
+            v0.new_empty((S, *v0.shape[:-1], R)), v0.new_empty((S, n), dtype=torch.float32))
+
+
+@torch.library.custom_op("attnres::lrid_kv_read_backward", mutates_args=())
+def lrid_kv_read_backward(
+    values: List[Tensor],
+    key_weight: Tensor,
+    keys: Tensor,
+    value_inv_rms: Tensor,
+    query: Optional[Tensor],
+    query_gate: Optional[Tensor],
+    query_dynamic: Optional[Tensor],
+    logit_bias: Optional[Tensor],
+    grad_output: Tensor,
+    normed_output: Tensor,
+    output_inv_rms: Tensor,
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    output_norm: int,
+    value_norm: bool,
+) -> tuple[List[Tensor], Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (dV list, d key_weight [R, d] fp32, dq, dgate, dq_dynamic, dbias)."""
+    values = list(values)
+    S, d = len(values), values[0].size(-1)
+    R = key_weight.size(0)
+    dtype = values[0].dtype
+    gv, gk, dq, dgate, dqd, dbias = _lrid_backward_impl(
+        values, list(keys.unbind(0)), query, query_gate, query_dynamic, logit_bias, grad_output, normed_output,
+        output_inv_rms, num_heads, logit_scale, key_norm, int(output_norm))
+    n = _ntok(values[0])
+    dk = torch.stack([g.reshape(n, R) for g in gk])  # [S, n, R]
+    w = key_weight.to(dtype)
+    dn = torch.matmul(dk, w)  # [S, n, d]: plain GEMM (cuBLAS)
+    rows, strides = _sources(values, d, dtype)
+    device = values[0].device
+    with torch.cuda.device(device):
+        rc = N.load().attnres_lrid_key_projection_backward(
+            S, n, d, R, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            N.ptr_array([g.data_ptr() for g in gv]), _ptr(dn), _ptr(dk), _ptr(keys.reshape(S, n, R)),
+            _ptr(value_inv_rms), int(bool(value_norm)), _stream_ptr(device))
+    N.check(rc, "attnres_lrid_key_projection_backward")
+    # d W = sum_s (inv_s * dK_s)^T @ V_s  (plain GEMMs, fp32 accumulation over sources)
+    dw = torch.zeros((R, d), device=device, dtype=torch.float32)
+    scale = value_inv_rms if value_norm else torch.ones_like(value_inv_rms)
+    for s in range(S):
+        a = (dk[s].float() * scale[s].unsqueeze(-1)).to(dtype)
+        dw += torch.matmul(a.t(), rows[s].reshape(n, d)).float()
+    e = values[0].new_empty((0,), dtype=torch.float32)
+    return (gv, dw, dq, dgate if dgate is not None else e, dqd if dqd is not None else e.clone(),
+            dbias if dbias is not None else e.clone())
+
+
+@lrid_kv_read_backward.register_fake
+def _(values, key_weight, keys, value_inv_rms, query, query_gate, query_dynamic, logit_bias, grad_output,
+      normed_output, output_inv_rms, num_heads, logit_scale, key_norm, output_norm, value_norm):
+    v0 = values[0]
+    n = v0.numel() // v0.size(-1)
+    H, R = int(num_heads), key_weight.size(0)
+    e = v0.new_empty((0,), dtype=torch.float32)
+    if query_dynamic is not None and query is None:
+        dq = v0.new_empty((n, H, R // H))
+    else:
+        dq = v0.new_empty((H, R // H), dtype=torch.float32)
+    gated = query_dynamic is not None and query is not None
+    return ([v.new_empty(v.shape) for v in values], key_weight.new_empty(key_weight.shape, dtype=torch.float32), dq,
+            v0.new_empty((H,), dtype=torch.float32) if gated else e,
+            v0.new_empty((n, H, R // H)) if gated else e.clone(),
+            v0.new_empty((len(values),), dtype=torch.float32) if logit_bias is not None else e.clone())
+
+
+def _lrid_kv_setup(ctx, inputs, output):
+    (values, key_weight, query, gate, qdyn, bias, num_heads, logit_scale, key_norm, output_norm,
+     value_norm) = inputs
+    out, oinv, keys, inv = output
+    ctx.has = (query is not None, gate is not None, qdyn is not None, bias is not None)
+    opt = [x for x in (query, gate, qdyn, bias) if x is not None]
+    ctx.save_for_backward(out, oinv, keys, inv, key_weight, *opt, *values)
+    ctx.n_opt = len(opt)
+    ctx.args = (int(num_heads), float(logit_scale), bool(key_norm), int(output_norm), bool(value_norm))
+
+
+def _lrid_kv_bwd(ctx, grad_out, grad_oinv, grad_keys, grad_inv):
+    saved = list(ctx.saved_tensors)
+    out, oinv, keys, inv, key_weight = saved[:5]
+    opt = iter(saved[5:5 + ctx.n_opt])
+    query, gate, qdyn, bias = (next(opt) if h else None for h in ctx.has)
+    values = saved[5 + ctx.n_opt:]
+    H, scale, key_norm, output_norm, value_norm = ctx.args
+    gv, dw, dq, dgate, dqd, dbias = lrid_kv_read_backward(
+        values, key_weight, keys, inv, query, gate, qdyn, bias, grad_out, out, oinv, H, scale, key_norm,
+        output_norm, value_norm)
+    g_query = g_gate = g_qdyn = g_bias = None
+    if qdyn is not None and query is None:
+        g_qdyn = dq.reshape(qdyn.shape).to(qdyn.dtype)
+    else:
+        g_query = dq.reshape(query.shape).to(query.dtype)
+        if qdyn is not None:
+            g_gate = dgate.reshape(gate.shape).to(gate.dtype)
+            g_qdyn = dqd.reshape(qdyn.shape).to(qdyn.dtype)
+    if bias is not None:
+        g_bias = dbias.reshape(bias.shape).to(bias.dtype)
+    return gv, dw.to(key_weight.dtype), g_query, g_gate, g_qdyn, g_bias, None, None, None, None, None
+
+
+lrid_kv_read.register_autograd(_lrid_kv_bwd, setup_context=_lrid_kv_setup)
+
+
+def lrid_attention_residual_read_key_from_value(
+    values,
+    key_weight: Tensor,
+    query: Tensor,
+    num_heads: int,
+    logit_scale: float,
+    key_norm: bool,
+    normalize_output: bool = False,
+    value_norm: bool = True,
+    source_counts=None,
+    source_logit_biases=None,
+    query_gate: Optional[Tensor] = None,
+    dynamic_query: Optional[Tensor] = None,
+) -> Tensor:
+    """LR-AttnRes read whose keys are projected from the values inside the op:
+    keys_s = rms_norm(V_s) @ key_weight^T (lrid_key_from_value, unshared;
+    model.py:344-356 with `value_key_proj.weight` as key_weight and
+    `lrid_key_value_norm` as value_norm). The projection runs on tcgen05
+    tensor cores for bf16/fp16 rows that allow it. Gradients flow to the values
+    (through both the read and the projection), key_weight and the query."""
+    values = _as_list(values)
+    if len(values) == 1:
+        return _norm(values[0]) if normalize_output else values[0]
+    dtype = values[0].dtype
+    bias = source_logit_bias(source_counts, source_logit_biases, len(values), values[0].device)
+    norm = _output_norm_mode(normalize_output, num_heads)
+    if dynamic_query is not None and query_gate is not None:
+        q, g, qd = query.to(dtype), query_gate.to(dtype), dynamic_query.to(dtype)
+    elif query.dim() == 4:
+        q, g, qd = None, None, query.to(dtype)
+    else:
+        q, g, qd = query.to(dtype), None, None
+    out, _, _, _ = lrid_kv_read(values, key_weight, q, g, qd, bias, int(num_heads), float(logit_scale),
+                                bool(key_norm), norm, bool(value_norm))
+    return out

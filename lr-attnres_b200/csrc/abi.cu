@@ -145,9 +145,11 @@ int attnres_device_status(unsigned* status, int reset) {
   if (!status) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "status is NULL");
   unsigned s1 = 0, s2 = 0;
   cudaError_t e = attnres::read_device_status(&s1, reset != 0);
+  unsigned s3 = 0;
   if (e == cudaSuccess) e = attnres::read_warp_status(&s2, reset != 0);
+  if (e == cudaSuccess) e = attnres::read_keyproj_status(&s3, reset != 0);
   if (e != cudaSuccess) return cuda_fail(e, "attnres_device_status");
-  *status = s1 | s2;
+  *status = s1 | s2 | s3;
   return ATTNRES_OK;
 }
 
@@ -422,6 +424,45 @@ int attnres_base_backward(int num_sources, int64_t num_tokens, int value_dim, in
   io.workspace = workspace;
   e = attnres::base_backward_launch(dtype, plan, io, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_base_backward launch");
+  return ATTNRES_OK;
+}
+
+int attnres_lrid_key_projection(int num_sources, int64_t num_tokens, int value_dim, int key_dim, int dtype,
+                                const void* const* values, const int64_t* value_row_strides,
+                                const void* weight, int64_t weight_row_stride, int value_norm,
+                                float value_eps, void* keys, float* inv_rms, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, 1, dtype, values, value_row_strides,
+                         nullptr, nullptr, false);
+  if (rc) return rc;
+  if (key_dim < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "key_dim=%d must be positive", key_dim);
+  if (!weight || weight_row_stride < value_dim)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "weight is NULL or its row stride is below value_dim");
+  if (num_tokens > 0 && !keys) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "keys is NULL");
+  if (value_norm && num_tokens > 0 && !inv_rms)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "value_norm needs an inv_rms output");
+  bool used_tc = false;
+  cudaError_t e = attnres::keyproj_launch(num_sources, num_tokens, value_dim, key_dim, dtype, values,
+                                          value_row_strides, weight, weight_row_stride, value_norm, value_eps,
+                                          keys, inv_rms, path_choice() != PATH_SIMT,
+                                          static_cast<cudaStream_t>(stream), &used_tc);
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_projection launch");
+  return ATTNRES_OK;
+}
+
+int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                         int dtype, const void* const* values,
+                                         const int64_t* value_row_strides, void* const* grad_values,
+                                         const void* grad_normed, const void* grad_keys, const void* keys,
+                                         const float* inv_rms, int value_norm, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, 1, dtype, values, value_row_strides,
+                         nullptr, nullptr, false);
+  if (rc) return rc;
+  if (num_tokens > 0 && (!grad_values || !grad_normed || !grad_keys || !keys || (value_norm && !inv_rms)))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "key projection backward: NULL buffer");
+  cudaError_t e = attnres::keyproj_bwd_combine_launch(num_sources, num_tokens, value_dim, key_dim, dtype, values,
+                                                      value_row_strides, grad_values, grad_normed, grad_keys,
+                                                      keys, inv_rms, value_norm, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_projection_backward launch");
   return ATTNRES_OK;
 }
 

@@ -147,3 +147,39 @@ def base_backward(values, query, key_norm, grad_output, logit_bias=None, output_
     if bias is not None:
         res["dbias"] = dbias
     return res
+
+
+def _kv_keys(values, weight, value_norm, value_eps):
+    """Key-from-value projection, double precision: keys_s = rms_norm(V_s) @ W^T
+    (reference model.py:344-356; norm = F.rms_norm over the last dim)."""
+    v = np.asarray(values, np.float64)
+    w = np.asarray(weight, np.float64)
+    inv = 1.0 / np.sqrt((v * v).mean(-1, keepdims=True) + value_eps) if value_norm else np.ones(v.shape[:-1] + (1,))
+    nhat = v * inv
+    return nhat @ w.T, inv, nhat
+
+
+def lrid_kv_forward(values, weight, num_heads, logit_scale, key_norm, value_norm=True,
+                    value_eps=float(np.finfo(np.float32).eps), **kw):
+    keys, _, _ = _kv_keys(values, weight, value_norm, value_eps)
+    return lrid_forward(values, keys.astype(np.float32), num_heads, logit_scale, key_norm, **kw)[0], keys
+
+
+def lrid_kv_backward(values, weight, num_heads, logit_scale, key_norm, grad_output, value_norm=True,
+                     value_eps=float(np.finfo(np.float32).eps), **kw):
+    """Read backward plus the projection backward:
+    dV += inv * (dK W - nhat * <dK, key>/d), dW = sum_s dK_s^T nhat_s."""
+    keys, inv, nhat = _kv_keys(values, weight, value_norm, value_eps)
+    res = lrid_backward(values, keys.astype(np.float32), num_heads, logit_scale, key_norm, grad_output, **kw)
+    dk = res["dK"]
+    w = np.asarray(weight, np.float64)
+    d = nhat.shape[-1]
+    dn = dk @ w
+    if value_norm:
+        c = (dk * keys).sum(-1, keepdims=True) / d
+        res["dV"] = res["dV"] + inv * (dn - nhat * c)
+    else:
+        res["dV"] = res["dV"] + dn
+    res["dW"] = np.einsum("snr,snd->rd", dk, nhat)
+    res["keys"] = keys
+    return res

@@ -33,6 +33,11 @@ CASES = [
     # rank-512 single head (test_fused_lrid_r512_single_head_eval_matches_torch, :916-931)
     dict(name="lrid_r512_h1", kind="lrid", S=3, B=1, T=3, D=1024, R=512, H=1, scale=1.0,
          key_norm=True, query="static", seed=26),
+    # keys projected from the values (lrid_key_from_value, model.py:344-356)
+    dict(name="lrid_kv_h2", kind="lrid_kv", S=5, B=2, T=5, D=128, R=32, H=2, scale=0.5,
+         key_norm=True, query="static", seed=31),
+    dict(name="lrid_kv_h1_nonorm", kind="lrid_kv", S=4, B=1, T=6, D=64, R=16, H=1, scale=0.25,
+         key_norm=True, query="static", value_norm=False, seed=32),
     # base AttnRes read, mirrors test_fused_base_attnres_matches_torch (:884-895)
     dict(name="base_small_kn", kind="base", S=5, B=2, T=5, D=64, key_norm=True, seed=21),
     dict(name="base_small_nokn", kind="base", S=5, B=2, T=5, D=64, key_norm=False, seed=22),
@@ -49,7 +54,7 @@ def case_inputs(case):
     S, N, D = case["S"], case["B"] * case["T"], case["D"]
     f = lambda *shape: rng.standard_normal(shape).astype(np.float32)  # noqa: E731
     inp = {"values": f(S, N, D)}
-    if case["kind"] == "lrid":
+    if case["kind"] in ("lrid", "lrid_kv"):
         H, R = case["H"], case["R"]
         inp["keys"] = f(S, N, R)
         inp["query"] = f(H, R // H)
@@ -57,6 +62,8 @@ def case_inputs(case):
         inp["gate"] = (0.1 + 0.2 * rng.standard_normal(H)).astype(np.float32)
     else:
         inp["query"] = (f(D) * np.float32(case.get("query_std", 1.0))).astype(np.float32)
+    if case["kind"] == "lrid_kv":
+        inp["key_weight"] = (rng.standard_normal((case["R"], D)) / np.sqrt(D)).astype(np.float32)
     inp["logit_bias"] = rng.standard_normal(S).astype(np.float32)
     inp["grad_output"] = f(N, D)
     return inp

@@ -43,6 +43,22 @@ def run_case(ref, case):
     values = [t(v.reshape(B, T, -1)) for v in inp["values"]]
     grad_out = torch.tensor(inp["grad_output"].reshape(B, T, -1), dtype=torch.float32)
     res = {}
+    if kind == "lrid_kv":
+        # keys from the values exactly as model.py:344-356 composes them
+        import torch.nn.functional as F
+
+        H = case["H"]
+        weight = t(inp["key_weight"])
+        query = t(inp["query"])
+        vn = case.get("value_norm", True)
+        keys = [F.linear(F.rms_norm(v, (v.size(-1),)) if vn else v, weight) for v in values]
+        out = ref.lrid_attention_residual_read(values, keys, query, H, case["scale"], case["key_norm"])
+        out.backward(grad_out)
+        res["out"] = out.detach().numpy().reshape(B * T, -1)
+        res["dV"] = np.stack([v.grad.numpy().reshape(B * T, -1) for v in values])
+        res["dW"] = weight.grad.numpy()
+        res["dq"] = query.grad.numpy().reshape(-1)
+        return res
     if kind == "lrid":
         H = case["H"]
         keys = [t(k.reshape(B, T, -1)) for k in inp["keys"]]

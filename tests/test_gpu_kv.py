@@ -1,0 +1,104 @@
+"""GPU parity of the key-from-value LRID read (BASELINE config 4 family):
+keys_s = rms_norm(V_s) @ W^T computed inside the op (tcgen05 tensor cores for
+bf16/fp16, CUDA cores otherwise), then the depth read; forward and backward
+(values through both paths, the key weight, the query) against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from cases import CASES, case_inputs
+from gpu_helpers import assert_close, dev_rows, rounded, to_np
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True, params=["auto", "simt"])
+def kernel_path(request, monkeypatch):
+    monkeypatch.setenv("ATTNRES_B200_PATH", request.param)
+    yield request.param
+    from attnres_b200 import _native
+
+    assert _native.device_status(reset=True) == 0
+
+
+def run_kv(inp, B, T, H, scale, key_norm, dtype, value_norm=True):
+    import attnres_b200 as A
+
+    values = [dev_rows(v, B, T, dtype) for v in inp["values"]]
+    w = torch.tensor(inp["key_weight"], device="cuda", dtype=torch.float32).to(dtype).requires_grad_(True)
+    q = torch.tensor(inp["query"], device="cuda", dtype=torch.float32, requires_grad=True)
+    out = A.lrid_attention_residual_read_key_from_value(values, w, q, H, scale, key_norm, value_norm=value_norm)
+    out.backward(dev_rows(inp["grad_output"], B, T, dtype, requires_grad=False))
+    torch.cuda.synchronize()
+    return {"out": to_np(out).reshape(B * T, -1),
+            "dV": np.stack([to_np(v.grad).reshape(B * T, -1) for v in values]),
+            "dW": to_np(w.grad), "dq": to_np(q.grad).reshape(-1)}
+
+
+def oracle_kv(inp, H, scale, key_norm, dtype, value_norm=True):
+    eps = float(torch.finfo(dtype).eps)
+    v, w = rounded(inp["values"], dtype), rounded(inp["key_weight"], dtype)
+    q = rounded(inp["query"], dtype)
+    g = rounded(inp["grad_output"], dtype)
+    out = oracle.lrid_kv_forward(v, w, H, scale, key_norm, value_norm=value_norm, value_eps=eps, query=q)[0]
+    res = oracle.lrid_kv_backward(v, w, H, scale, key_norm, g, value_norm=value_norm, value_eps=eps, query=q)
+    res["out"] = out
+    return res
+
+
+def compare(res, ref, dtype, n):
+    assert_close("out", res["out"], ref["out"], dtype)
+    assert_close("dV", res["dV"], ref["dV"], dtype)
+    assert_close("dW", res["dW"], ref["dW"], dtype, sum_terms=n)
+    assert_close("dq", res["dq"], ref["dq"], dtype, sum_terms=n)
+
+
+KV_CASES = [c for c in CASES if c["kind"] == "lrid_kv"]
+
+
+@pytest.mark.parametrize("case", KV_CASES, ids=[c["name"] for c in KV_CASES])
+def test_kv_golden_cases_fp32(case):
+    inp = case_inputs(case)
+    vn = case.get("value_norm", True)
+    res = run_kv(inp, case["B"], case["T"], case["H"], case["scale"], case["key_norm"], torch.float32, vn)
+    ref = oracle_kv(inp, case["H"], case["scale"], case["key_norm"], torch.float32, vn)
+    compare(res, ref, torch.float32, case["B"] * case["T"])
+
+
+def make(S, N, D, R, H, seed):
+    rng = np.random.default_rng(seed)
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    return {"values": f(S, N, D), "key_weight": (f(R, D) / np.sqrt(D)).astype(np.float32),
+            "query": (f(H, R // H) * 0.5).astype(np.float32), "grad_output": f(N, D)}
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("S,N,D,R,value_norm", [
+    (3, 300, 256, 64, True),     # partial last 128-row tile
+    (17, 260, 2048, 64, True),   # BASELINE config-4 row shape (S=17, d=2048, R=64)
+    (4, 129, 128, 32, False),    # no value norm, R=32
+    (2, 1000, 512, 128, True),   # R=128, several tiles per source
+])
+def test_key_projection_matches_oracle(dtype, S, N, D, R, value_norm):
+    """The projection alone: keys and the value inv-rms it saves."""
+    from attnres_b200.ops import _kv_project
+
+    inp = make(S, N, D, R, 1, seed=S * 7 + R)
+    v = [torch.tensor(x, device="cuda").to(dtype) for x in inp["values"]]
+    w = torch.tensor(inp["key_weight"], device="cuda").to(dtype)
+    keys, inv = _kv_project(v, w, value_norm)
+    torch.cuda.synchronize()
+    ref_keys, ref_inv, _ = oracle._kv_keys(rounded(inp["values"], dtype), rounded(inp["key_weight"], dtype),
+                                           value_norm, float(torch.finfo(dtype).eps))
+    assert_close("keys", to_np(keys), ref_keys, dtype)
+    if value_norm:
+        assert_close("inv_rms", to_np(inv), ref_inv[..., 0], torch.float32)
+
+
+@pytest.mark.parametrize("S,N,D,R,H", [(17, 150, 2048, 64, 1), (5, 200, 256, 64, 2)])
+def test_kv_read_bf16(S, N, D, R, H):
+    inp = make(S, N, D, R, H, seed=N)
+    res = run_kv(inp, 1, N, H, 1.0 / np.sqrt(R // H), True, torch.bfloat16)
+    ref = oracle_kv(inp, H, 1.0 / np.sqrt(R // H), True, torch.bfloat16)
+    compare(res, ref, torch.bfloat16, N)

@@ -25,6 +25,12 @@ def oracle_case(case):
         else:
             norm = oracle.NORM_PER_HEAD if case["H"] == 1 else oracle.NORM_ROW
     bias = inp["logit_bias"] if case.get("bias") else None
+    if case["kind"] == "lrid_kv":
+        vn = case.get("value_norm", True)
+        args = (inp["values"], inp["key_weight"], case["H"], case["scale"], case["key_norm"])
+        out = oracle.lrid_kv_forward(*args, value_norm=vn, query=inp["query"])[0]
+        grads = oracle.lrid_kv_backward(*args, inp["grad_output"], value_norm=vn, query=inp["query"])
+        return out, grads
     if case["kind"] == "base":
         out, _ = oracle.base_forward(inp["values"], inp["query"], case["key_norm"], bias, norm)
         grads = oracle.base_backward(inp["values"], inp["query"], case["key_norm"], inp["grad_output"], bias, norm)
@@ -64,6 +70,8 @@ def test_oracle_matches_reference_golden(case):
                 _close(name + "_sum", got.sum(axis=(1, 2)), gold[name + "_sum"], scale=10.0)
                 got = got[:, :keep]
             _close(name, got, gold[name])
+    if "dW" in gold:
+        _close("dW", grads["dW"], gold["dW"], scale=4.0)
     for name in ("dq", "dgate", "dq_dynamic", "dbias"):
         if name in gold:
             _close(name, grads[name].reshape(gold[name].shape), gold[name], scale=4.0)
