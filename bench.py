@@ -37,6 +37,8 @@ CONFIGS = {
     "config2": dict(S=9, B=8, T=2048, D=1024, R=64, H=1, scale=1 / 8, query="static"),
     # BASELINE config 3 (gated hybrid query), reported with --config config3
     "config3": dict(S=13, B=16, T=2048, D=2048, R=64, H=4, scale=1 / 4, query="gated"),
+    # keys projected from the values in-op (rms_norm(V) @ W_k^T, tcgen05)
+    "config4": dict(S=17, B=32, T=4096, D=2048, R=64, H=1, scale=1 / 8, query="static", kv=True),
     # small case for ncu captures (inputs still > L2)
     "small": dict(S=9, B=4, T=2048, D=1024, R=64, H=1, scale=1 / 8, query="static"),
 }
@@ -59,6 +61,9 @@ def parse():
 def algorithmic_bytes(c, esz=2):
     """Each input read once, each output written once (per token)."""
     S, D, R = c["S"], c["D"], c["R"]
+    if c.get("kv"):
+        # forward reads V, writes out; backward reads V and g, writes dV (keys stay internal)
+        return S * D * esz + D * esz, S * D * esz + D * esz + S * D * esz
     q_tok = R * esz if c["query"] != "static" else 0
     fwd = S * (D + R) * esz + q_tok + D * esz
     bwd = D * esz + S * (D + R) * esz + q_tok + S * (D + R) * esz + q_tok
@@ -222,7 +227,9 @@ def make_inputs(c, device, torch, seed):
     bf = torch.bfloat16
     x = {
         "values": [torch.randn(B, T, D, device=device, dtype=bf, generator=g) for _ in range(S)],
-        "keys": [torch.randn(B, T, R, device=device, dtype=bf, generator=g) for _ in range(S)],
+        "keys": ([torch.randn(B, T, R, device=device, dtype=bf, generator=g) for _ in range(S)]
+                 if not c.get("kv") else None),
+        "weight": ((torch.randn(R, D, device=device, generator=g) / D ** 0.5).to(bf) if c.get("kv") else None),
         "query": (torch.randn(H, R // H, device=device, generator=g) * 0.02).to(bf),
         "grad": torch.randn(B, T, D, device=device, dtype=bf, generator=g),
         "gate": None, "qdyn": None,
@@ -258,10 +265,21 @@ def main():
     gated = c["query"] == "gated"
     q, gate, qdyn = x["query"], x["gate"], x["qdyn"]
 
+    kv = bool(c.get("kv"))
+
     def fwd():
+        if kv:
+            return ops.lrid_kv_read(x["values"], x["weight"], q, gate, qdyn, None, H, scale, True, 0, True)
         return ops.lrid_read(x["values"], x["keys"], q, gate, qdyn, None, H, scale, True, 0)
 
-    def bwd(out, inv):
+    def bwd(*fo):
+        if kv:
+            out, inv, keys, vinv, alpha = fo
+            r = ops.lrid_kv_read_backward(x["values"], x["weight"], keys, vinv, alpha, q, gate, qdyn, None,
+                                          x["grad"], out, inv, H, scale, True, 0, True)
+            # (dV, dW, dq, dgate, ...) -> keep dq / dgate at the same positions as the plain read
+            return r[0], r[1], r[2], r[3]
+        out, inv = fo
         return ops.lrid_read_backward(x["values"], x["keys"], q, gate, qdyn, None, x["grad"], out, inv,
                                       H, scale, True, 0)
 
@@ -270,7 +288,7 @@ def main():
     def allreduce(dq, dgate):
         # the only cross-GPU step: one bucketed NCCL all-reduce of the summed grads
         if world > 1:
-            allreduce_param_grads([dq, dgate] if gated else [dq])
+            allreduce_param_grads([dq] + ([dgate] if gated else []) + ([dw] if kv else []))
 
     stream = torch.cuda.Stream(device)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
@@ -278,8 +296,7 @@ def main():
     if args.profile:
         with torch.cuda.stream(stream):
             for _ in range(args.warmup + args.steps):
-                out, inv = fwd()
-                bwd(out, inv)
+                bwd(*fwd())
         torch.cuda.synchronize()
         if rank == 0:
             print(json.dumps({"profile_run": True, "config": args.config}), flush=True)
@@ -288,15 +305,15 @@ def main():
     # ---- capture fwd and bwd as two CUDA graphs (static buffers) ----------
     with torch.cuda.stream(stream):
         for _ in range(3):  # allocator warm-up outside capture
-            out, inv = fwd()
-            res = bwd(out, inv)
+            res = bwd(*fwd())
     torch.cuda.synchronize()
     g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_fwd, stream=stream):
-        out, inv = fwd()
+        fo = fwd()
     with torch.cuda.graph(g_bwd, stream=stream):
-        res = bwd(out, inv)
+        res = bwd(*fo)
     dq, dgate = res[2], res[3]
+    dw = res[1] if kv else None
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
@@ -381,11 +398,38 @@ def main():
 
     # ---- e2e: public API, pinned host buffers, copies inside timed region --
     e2e = None
-    if args.e2e_steps > 0:
+    if args.e2e_steps > 0 and not kv:
         e2e = run_e2e(args, c, x, device, torch, dist, world)
 
+    proj = None
+    if kv:
+        # the tcgen05 key projection alone, for its TFLOP/s against the tensor peak
+        from attnres_b200.ops import _kv_project
+
+        with torch.cuda.stream(stream):
+            _kv_project(x["values"], x["weight"], True)
+        torch.cuda.synchronize()
+        g_proj = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_proj, stream=stream):
+            _kv_project(x["values"], x["weight"], True)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            g_proj.replay()
+            p0.record(stream)
+            for _ in range(10):
+                g_proj.replay()
+            p1.record(stream)
+        torch.cuda.synchronize()
+        pms = p0.elapsed_time(p1) / 10
+        flops = 2.0 * c["S"] * tokens * c["D"] * c["R"]
+        tpeak = float(peaks.get("bf16_tflops", 1590.0))
+        pbytes = c["S"] * tokens * (c["D"] + c["R"]) * 2
+        proj = {"kernel": "keyproj_tc_kernel (tcgen05)", "ms": pms, "tflops": flops / pms / 1e9,
+                "peak_tflops": tpeak, "frac_tensor": flops / pms / 1e9 / tpeak,
+                "gbs": pbytes / pms / 1e6, "frac_hbm": pbytes / pms / 1e6 / hbm}
+
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not kv:
         r, cores, sample = cpu_oracle_rate(c, target_s=12.0)
         cpu = {"value": r, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
@@ -398,7 +442,7 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) values/keys/grads, query N(0,0.02))",
             "config": config_block(c, args),
             "roofline": {
-                "kernel": "backward LRID read (lrid_stream_kernel for this row shape)", "bound": "hbm",
+                "kernel": ("backward (read backward + projection backward)" if kv else "backward LRID read (lrid_stream_kernel for this row shape)"), "bound": "hbm",
                 "achieved": bwd_gbs, "peak": hbm, "unit": "GB/s", "frac": bwd_gbs / hbm,
                 "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs" if peak_src == "measured" else "fallback 6650 GB/s",
                 "traffic": (traffic.get("backward", 0) * tokens) if (traffic and args.config == "config2") else None,
@@ -407,6 +451,7 @@ def main():
                 "forward": {"achieved": fwd_gbs, "frac": fwd_gbs / hbm, "kernel_ms": fwd_ms,
                             "algorithmic_bytes_per_token": fwd_b},
                 "step": {"achieved": step_gbs, "frac": step_gbs / hbm},
+                "projection": proj,
             },
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -122,7 +122,8 @@ size_t attnres_lrid_backward_workspace_bytes(int num_sources, int64_t num_tokens
 /*
  * LRID read, backward. Replaces attnres::lrid_read_list_backward (attnres_ops.py:4725).
  * Softmax weights are recomputed from the keys (same arithmetic as the forward).
- *   grad_values[s] : dtype [N, d] dense  = alpha * g'            (g' = output-norm backward of g)
+ *   grad_values[s] : dtype [N, d] dense  = alpha * g'            (g' = output-norm backward of g);
+ *                    grad_values == NULL skips these writes (callers that form dV themselves)
  *   grad_keys[s]   : dtype [N, R] dense  = key-norm backward of dlogit*scale*q
  *   grad_query     : STATIC/GATED: float [H, dk] summed over tokens (deterministic order)
  *                    DYNAMIC     : dtype [N, H, dk] per token
@@ -196,18 +197,23 @@ int attnres_lrid_key_projection(int num_sources, int64_t num_tokens, int value_d
                                 float value_eps, void* keys, float* inv_rms, void* stream);
 
 /*
- * Backward of the value rms-norm in the key projection, accumulated into
+ * Backward of the value rms-norm in the key projection, combined into
  * grad_values (dense [N, d] each):
- *   grad_values[s][n] += inv * (dn - (V*inv) * <dK, key> / d)
- * grad_normed = dK @ W: dtype [S][N][d]; grad_keys = dK: dtype [S][N][R];
- * keys / inv_rms: the forward's outputs. (The weight gradient
- * sum_s (inv_s * dK_s)^T @ V_s is a plain GEMM left to the caller.)
+ *   grad_values[s][n] = base + inv * (dn - (V*inv) * <dK, key> / d)
+ * grad_normed = dn = dK @ W: dtype [S][N][d]; grad_keys = dK: dtype [S][N][R];
+ * keys / inv_rms: the forward's outputs. base = alpha[n,h,s] * grad_output[n]
+ * when grad_output (dtype [N, d]) and alpha (float [N, H, S], the forward's
+ * softmax weights) are given -- the read backward then runs with
+ * grad_values == NULL -- otherwise the current grad_values (read-modify-write).
+ * The weight gradient sum_s (inv_s * dK_s)^T @ V_s is a plain GEMM left to
+ * the caller. Replaces the autograd backward of model.py:344-356.
  */
 int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
-                                         int dtype, const void* const* values,
+                                         int num_heads, int dtype, const void* const* values,
                                          const int64_t* value_row_strides, void* const* grad_values,
                                          const void* grad_normed, const void* grad_keys, const void* keys,
-                                         const float* inv_rms, int value_norm, void* stream);
+                                         const float* inv_rms, const void* grad_output, const float* alpha,
+                                         int value_norm, void* stream);
 
 /*
  * Base AttnRes read, forward (keys are the values themselves).

@@ -98,7 +98,7 @@ def load(path=None):
     L.attnres_lrid_key_projection.restype = I
     L.attnres_lrid_key_projection.argtypes = [I, I64, I, I, I, PP, PI64, P, I64, I, F, P, P, P]
     L.attnres_lrid_key_projection_backward.restype = I
-    L.attnres_lrid_key_projection_backward.argtypes = [I, I64, I, I, I, PP, PI64, PP, P, P, P, P, I, P]
+    L.attnres_lrid_key_projection_backward.argtypes = [I, I64, I, I, I, I, PP, PI64, PP, P, P, P, P, P, P, I, P]
     L.attnres_base_forward.restype = I
     L.attnres_base_forward.argtypes = [
         I, I64, I, I, PP, PI64, P, I, F, P, I, F, P, P, P,

@@ -175,7 +175,7 @@ def _query_pack(query, gate, query_dynamic, H, R, n, dtype):
 
 def _lrid_backward_impl(values, keys, query, query_gate, query_dynamic, logit_bias, grad_output,
                         normed_output, output_inv_rms, num_heads, logit_scale, key_norm,
-                        output_norm, need_bias_grad=True):
+                        output_norm, need_bias_grad=True, write_dv=True):
     S = len(values)
     H = int(num_heads)
     d = values[0].size(-1)
@@ -216,7 +216,7 @@ def _lrid_backward_impl(values, keys, query, query_gate, query_dynamic, logit_bi
             float(logit_scale), int(bool(key_norm)), F32_EPS, _ptr(bias),
             int(output_norm), float(torch.finfo(dtype).eps),
             _ptr(grad_output), _ptr(y), _ptr(output_inv_rms) if y is not None else None,
-            N.ptr_array([t.data_ptr() for t in grad_values]),
+            N.ptr_array([t.data_ptr() for t in grad_values]) if write_dv else None,
             N.ptr_array([t.data_ptr() for t in grad_keys]),
             _ptr(dq), _ptr(dgate), _ptr(dqd), _ptr(dbias),
             _ptr(ws), ws.numel(), _stream_ptr(device),
@@ -742,13 +742,16 @@ def lrid_kv_read(
     key_norm: bool,
     output_norm: int,
     value_norm: bool,
-) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-    """Returns (out, output_inv_rms, keys [S, *lead, R], value_inv_rms [S, N])."""
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (out, output_inv_rms, keys [S, *lead, R], value_inv_rms [S, N],
+    alpha [N, H, S] -- the softmax weights, kept so the backward forms dV in
+    one pass; [1] when the output is normalised)."""
     values = list(values)
     keys, inv = _kv_project(values, key_weight, value_norm)
-    out, oinv, _, _ = _lrid_forward_impl(values, list(keys.unbind(0)), query, query_gate, query_dynamic,
-                                         logit_bias, num_heads, logit_scale, key_norm, int(output_norm), False)
-    return out, oinv, keys, inv
+    save = int(output_norm) == N.NORM_NONE
+    out, oinv, alpha, _ = _lrid_forward_impl(values, list(keys.unbind(0)), query, query_gate, query_dynamic,
+                                             logit_bias, num_heads, logit_scale, key_norm, int(output_norm), save)
+    return out, oinv, keys, inv, alpha
 
 
 @lrid_kv_read.register_fake
@@ -758,8 +761,10 @@ def _(values, key_weight, query, query_gate, query_dynamic, logit_bias, num_head
     n = v0.numel() // v0.size(-1)
     S, R = len(values), key_weight.size(0)
     shape = {N.NORM_PER_HEAD: (n, int(num_heads)), N.NORM_ROW: (n,)}.get(int(output_norm), (1,))
+    aux = (n, int(num_heads), S) if int(output_norm) == N.NORM_NONE else (1,)
     return (v0.new_empty(v0.shape), v0.new_empty(shape, dtype=torch.float32),
-            v0.new_empty((S, *v0.shape[:-1], R)), v0.new_empty((S, n), dtype=torch.float32))
+            v0.new_empty((S, *v0.shape[:-1], R)), v0.new_empty((S, n), dtype=torch.float32),
+            v0.new_empty(aux, dtype=torch.float32))
 
 
 @torch.library.custom_op("attnres::lrid_kv_read_backward", mutates_args=())
@@ -768,6 +773,7 @@ def lrid_kv_read_backward(
     key_weight: Tensor,
     keys: Tensor,
     value_inv_rms: Tensor,
+    alpha: Tensor,
     query: Optional[Tensor],
     query_gate: Optional[Tensor],
     query_dynamic: Optional[Tensor],
@@ -786,10 +792,12 @@ def lrid_kv_read_backward(
     S, d = len(values), values[0].size(-1)
     R = key_weight.size(0)
     dtype = values[0].dtype
+    one_pass = int(output_norm) == N.NORM_NONE and alpha.numel() > 1
     gv, gk, dq, dgate, dqd, dbias = _lrid_backward_impl(
         values, list(keys.unbind(0)), query, query_gate, query_dynamic, logit_bias, grad_output, normed_output,
-        output_inv_rms, num_heads, logit_scale, key_norm, int(output_norm))
+        output_inv_rms, num_heads, logit_scale, key_norm, int(output_norm), write_dv=not one_pass)
     n = _ntok(values[0])
+    g_rows = grad_output.to(dtype).reshape(n, d).contiguous() if one_pass else None
     dk = torch.stack([g.reshape(n, R) for g in gk])  # [S, n, R]
     w = key_weight.to(dtype)
     dn = torch.matmul(dk, w)  # [S, n, d]: plain GEMM (cuBLAS)
@@ -797,9 +805,10 @@ def lrid_kv_read_backward(
     device = values[0].device
     with torch.cuda.device(device):
         rc = N.load().attnres_lrid_key_projection_backward(
-            S, n, d, R, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
-            N.ptr_array([g.data_ptr() for g in gv]), _ptr(dn), _ptr(dk), _ptr(keys.reshape(S, n, R)),
-            _ptr(value_inv_rms), int(bool(value_norm)), _stream_ptr(device))
+            S, n, d, R, int(num_heads), _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]),
+            N.i64_array(strides), N.ptr_array([g.data_ptr() for g in gv]), _ptr(dn), _ptr(dk),
+            _ptr(keys.reshape(S, n, R)), _ptr(value_inv_rms), _ptr(g_rows),
+            _ptr(alpha.contiguous()) if one_pass else None, int(bool(value_norm)), _stream_ptr(device))
     N.check(rc, "attnres_lrid_key_projection_backward")
     # d W = sum_s (inv_s * dK_s)^T @ V_s  (plain GEMMs, fp32 accumulation over sources)
     dw = torch.zeros((R, d), device=device, dtype=torch.float32)
@@ -813,7 +822,7 @@ def lrid_kv_read_backward(
 
 
 @lrid_kv_read_backward.register_fake
-def _(values, key_weight, keys, value_inv_rms, query, query_gate, query_dynamic, logit_bias, grad_output,
+def _(values, key_weight, keys, value_inv_rms, alpha, query, query_gate, query_dynamic, logit_bias, grad_output,
       normed_output, output_inv_rms, num_heads, logit_scale, key_norm, output_norm, value_norm):
     v0 = values[0]
     n = v0.numel() // v0.size(-1)
@@ -833,23 +842,23 @@ def _(values, key_weight, keys, value_inv_rms, query, query_gate, query_dynamic,
 def _lrid_kv_setup(ctx, inputs, output):
     (values, key_weight, query, gate, qdyn, bias, num_heads, logit_scale, key_norm, output_norm,
      value_norm) = inputs
-    out, oinv, keys, inv = output
+    out, oinv, keys, inv, alpha = output
     ctx.has = (query is not None, gate is not None, qdyn is not None, bias is not None)
     opt = [x for x in (query, gate, qdyn, bias) if x is not None]
-    ctx.save_for_backward(out, oinv, keys, inv, key_weight, *opt, *values)
+    ctx.save_for_backward(out, oinv, keys, inv, alpha, key_weight, *opt, *values)
     ctx.n_opt = len(opt)
     ctx.args = (int(num_heads), float(logit_scale), bool(key_norm), int(output_norm), bool(value_norm))
 
 
-def _lrid_kv_bwd(ctx, grad_out, grad_oinv, grad_keys, grad_inv):
+def _lrid_kv_bwd(ctx, grad_out, grad_oinv, grad_keys, grad_inv, grad_alpha):
     saved = list(ctx.saved_tensors)
-    out, oinv, keys, inv, key_weight = saved[:5]
-    opt = iter(saved[5:5 + ctx.n_opt])
+    out, oinv, keys, inv, alpha, key_weight = saved[:6]
+    opt = iter(saved[6:6 + ctx.n_opt])
     query, gate, qdyn, bias = (next(opt) if h else None for h in ctx.has)
-    values = saved[5 + ctx.n_opt:]
+    values = saved[6 + ctx.n_opt:]
     H, scale, key_norm, output_norm, value_norm = ctx.args
     gv, dw, dq, dgate, dqd, dbias = lrid_kv_read_backward(
-        values, key_weight, keys, inv, query, gate, qdyn, bias, grad_out, out, oinv, H, scale, key_norm,
+        values, key_weight, keys, inv, alpha, query, gate, qdyn, bias, grad_out, out, oinv, H, scale, key_norm,
         output_norm, value_norm)
     g_query = g_gate = g_qdyn = g_bias = None
     if qdyn is not None and query is None:
@@ -899,6 +908,6 @@ def lrid_attention_residual_read_key_from_value(
         q, g, qd = None, None, query.to(dtype)
     else:
         q, g, qd = query.to(dtype), None, None
-    out, _, _, _ = lrid_kv_read(values, key_weight, q, g, qd, bias, int(num_heads), float(logit_scale),
-                                bool(key_norm), norm, bool(value_norm))
+    out, _, _, _, _ = lrid_kv_read(values, key_weight, q, g, qd, bias, int(num_heads), float(logit_scale),
+                                   bool(key_norm), norm, bool(value_norm))
     return out

@@ -255,14 +255,13 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
   if (rc) return rc;
   if ((rc = check_query(query_mode, query, query_gate, query_dynamic))) return rc;
   if ((rc = check_norm(output_norm, true))) return rc;
-  if (!grad_values || !grad_keys)
-    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_values/grad_keys is NULL");
+  if (!grad_keys) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_keys is NULL");
   if (num_tokens > 0) {
     if (!grad_output) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_output is NULL");
     if (output_norm != ATTNRES_NORM_NONE && (!normed_output || !output_inv_rms))
       return fail(ATTNRES_ERR_INVALID_ARGUMENT, "output norm backward needs normed_output and output_inv_rms");
     for (int s = 0; s < num_sources; ++s)
-      if (!grad_values[s] || !grad_keys[s])
+      if ((grad_values && !grad_values[s]) || !grad_keys[s])
         return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_values[%d]/grad_keys[%d] is NULL", s, s);
   }
   if (!grad_query) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_query is NULL");
@@ -273,7 +272,7 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
   int n_extra = 0;
   extra[n_extra++] = grad_output;
   extra[n_extra++] = output_norm != ATTNRES_NORM_NONE ? normed_output : nullptr;
-  for (int s = 0; s < num_sources; ++s) extra[n_extra++] = grad_values[s];
+  for (int s = 0; s < num_sources && grad_values; ++s) extra[n_extra++] = grad_values[s];
   const bool vec = values_vectorizable(num_sources, esz, values, value_row_strides, extra, n_extra);
   attnres::LridPlan plan;
   const char* why = "";
@@ -450,18 +449,24 @@ int attnres_lrid_key_projection(int num_sources, int64_t num_tokens, int value_d
 }
 
 int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
-                                         int dtype, const void* const* values,
+                                         int num_heads, int dtype, const void* const* values,
                                          const int64_t* value_row_strides, void* const* grad_values,
                                          const void* grad_normed, const void* grad_keys, const void* keys,
-                                         const float* inv_rms, int value_norm, void* stream) {
-  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, 1, dtype, values, value_row_strides,
-                         nullptr, nullptr, false);
+                                         const float* inv_rms, const void* grad_output, const float* alpha,
+                                         int value_norm, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values,
+                         value_row_strides, nullptr, nullptr, false);
   if (rc) return rc;
+  if (num_heads < 1 || value_dim % num_heads)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "value_dim must divide by num_heads");
   if (num_tokens > 0 && (!grad_values || !grad_normed || !grad_keys || !keys || (value_norm && !inv_rms)))
     return fail(ATTNRES_ERR_INVALID_ARGUMENT, "key projection backward: NULL buffer");
-  cudaError_t e = attnres::keyproj_bwd_combine_launch(num_sources, num_tokens, value_dim, key_dim, dtype, values,
-                                                      value_row_strides, grad_values, grad_normed, grad_keys,
-                                                      keys, inv_rms, value_norm, static_cast<cudaStream_t>(stream));
+  if ((grad_output == nullptr) != (alpha == nullptr))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_output and alpha go together");
+  cudaError_t e = attnres::keyproj_bwd_combine_launch(num_sources, num_tokens, value_dim, key_dim, num_heads,
+                                                      dtype, values, value_row_strides, grad_values,
+                                                      grad_normed, grad_keys, keys, inv_rms, grad_output,
+                                                      alpha, value_norm, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_projection_backward launch");
   return ATTNRES_OK;
 }

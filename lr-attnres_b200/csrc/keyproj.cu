@@ -316,22 +316,27 @@ __global__ void __launch_bounds__(256) keyproj_simt_kernel(const __grid_constant
   if (lane == 0 && a.inv_rms) a.inv_rms[row] = inv;
 }
 
-// Backward of the value rms-norm of the projection, added into grad_values:
-//   dV[s][t] += inv * (dn - (V * inv) * <dK, key> / d),   dn = dK @ W (given)
-// (<dn, V*inv> = <dK, key> because key = (V*inv) @ W^T.)
+// Backward of the value rms-norm of the projection, combined into grad_values:
+//   dV[s][t] = base + inv * (dn - (V * inv) * <dK, key> / d),   dn = dK @ W (given)
+// (<dn, V*inv> = <dK, key> because key = (V*inv) @ W^T). base is either the
+// read backward's alpha * g (alpha [N,H,S] saved by the forward, g the upstream
+// gradient: the read then skips its own dV writes) or the current grad_values
+// (read-modify-write). One warp per (source, token) row, VEC-wide packs.
 struct KeyProjBwdArgs {
   const void* v[ATTNRES_MAX_SOURCES];
   long long vs[ATTNRES_MAX_SOURCES];
-  void* gv[ATTNRES_MAX_SOURCES];  // [N, d] dense, accumulated in place
+  void* gv[ATTNRES_MAX_SOURCES];  // [N, d] dense
   const void* dn;                 // [S][N][d] dense
   const void* dk;                 // [S][N][R]
   const void* keys;               // [S][N][R]
   const float* inv_rms;           // [S][N]
+  const void* g;                  // [N, d] upstream gradient, or null (read-modify-write)
+  const float* alpha;             // [N, H, S] softmax weights, with g
   long long N;
-  int S, d, R, value_norm;
+  int S, d, R, H, value_norm;
 };
 
-template <typename T>
+template <typename T, int VEC>
 __global__ void __launch_bounds__(256) keyproj_bwd_combine_kernel(const __grid_constant__ KeyProjBwdArgs a) {
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -342,16 +347,32 @@ __global__ void __launch_bounds__(256) keyproj_bwd_combine_kernel(const __grid_c
   const T* kk = static_cast<const T*>(a.keys) + row * a.R;
   float c = 0.f;
   for (int r = lane; r < a.R; r += 32) c = fmaf(Elem<T>::to_f(dk[r]), Elem<T>::to_f(kk[r]), c);
-  c = warp_sum(c) / a.d;
+  c = a.value_norm ? warp_sum(c) / a.d : 0.f;
   const float inv = a.value_norm ? a.inv_rms[row] : 1.f;
-  if (!a.value_norm) c = 0.f;
   const T* v = static_cast<const T*>(a.v[s]) + t * a.vs[s];
   const T* dn = static_cast<const T*>(a.dn) + row * a.d;
+  const T* g = a.g ? static_cast<const T*>(a.g) + t * a.d : nullptr;
   T* gv = static_cast<T*>(a.gv[s]) + t * a.d;
-  for (int j = lane; j < a.d; j += 32) {
-    const float y = Elem<T>::to_f(v[j]) * inv;
-    const float add = inv * (Elem<T>::to_f(dn[j]) - y * c);
-    gv[j] = Elem<T>::from_f(Elem<T>::to_f(gv[j]) + add);
+  const int dv = a.d / a.H;
+  for (int j = lane * VEC; j < a.d; j += 32 * VEC) {
+    const Pack<T, VEC> vp = load_stream<T, VEC>(v + j);
+    const Pack<T, VEC> np = load_stream<T, VEC>(dn + j);
+    Pack<T, VEC> bp;
+    float al = 0.f;
+    if (g) {
+      bp = load_pack<T, VEC>(g + j);
+      al = a.alpha[(t * a.H + j / dv) * a.S + s];
+    } else {
+      bp = load_pack<T, VEC>(gv + j);
+    }
+    float o[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float base = g ? al * Elem<T>::to_f(bp.e[e]) : Elem<T>::to_f(bp.e[e]);
+      const float y = Elem<T>::to_f(vp.e[e]) * inv;
+      o[e] = base + inv * (Elem<T>::to_f(np.e[e]) - y * c);
+    }
+    store_pack<T, VEC>(gv + j, o);
   }
 }
 
@@ -472,32 +493,49 @@ cudaError_t keyproj_launch(int S, long long N, int d, int R, int dtype, const vo
   return cudaGetLastError();
 }
 
-cudaError_t keyproj_bwd_combine_launch(int S, long long N, int d, int R, int dtype, const void* const* values,
-                                       const int64_t* vstr, void* const* grad_values, const void* dn,
-                                       const void* dk, const void* keys, const float* inv_rms, int value_norm,
-                                       cudaStream_t st) {
+cudaError_t keyproj_bwd_combine_launch(int S, long long N, int d, int R, int H, int dtype,
+                                       const void* const* values, const int64_t* vstr,
+                                       void* const* grad_values, const void* dn, const void* dk,
+                                       const void* keys, const float* inv_rms, const void* g,
+                                       const float* alpha, int value_norm, cudaStream_t st) {
   const long long rows = static_cast<long long>(S) * N;
   if (rows == 0) return cudaSuccess;
   KeyProjBwdArgs a{};
+  const int esz = dtype == ATTNRES_DTYPE_F32 ? 4 : 2;
+  const int full = 16 / esz;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  bool vec = (d % full) == 0 && (d / H) % full == 0 && al16(dn) && (!g || al16(g));
   for (int s = 0; s < S; ++s) {
     a.v[s] = values[s];
     a.vs[s] = vstr[s];
     a.gv[s] = grad_values[s];
+    vec = vec && al16(values[s]) && (vstr[s] * esz) % 16 == 0 && al16(grad_values[s]);
   }
   a.dn = dn;
   a.dk = dk;
   a.keys = keys;
   a.inv_rms = inv_rms;
+  a.g = g;
+  a.alpha = alpha;
   a.N = N;
   a.S = S;
   a.d = d;
   a.R = R;
+  a.H = H;
   a.value_norm = value_norm;
   const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
   switch (dtype) {
-    case ATTNRES_DTYPE_F32: keyproj_bwd_combine_kernel<float><<<grid, 256, 0, st>>>(a); break;
-    case ATTNRES_DTYPE_F16: keyproj_bwd_combine_kernel<__half><<<grid, 256, 0, st>>>(a); break;
-    default: keyproj_bwd_combine_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
+    case ATTNRES_DTYPE_F32:
+      if (vec) keyproj_bwd_combine_kernel<float, 4><<<grid, 256, 0, st>>>(a);
+      else keyproj_bwd_combine_kernel<float, 1><<<grid, 256, 0, st>>>(a);
+      break;
+    case ATTNRES_DTYPE_F16:
+      if (vec) keyproj_bwd_combine_kernel<__half, 8><<<grid, 256, 0, st>>>(a);
+      else keyproj_bwd_combine_kernel<__half, 1><<<grid, 256, 0, st>>>(a);
+      break;
+    default:
+      if (vec) keyproj_bwd_combine_kernel<__nv_bfloat16, 8><<<grid, 256, 0, st>>>(a);
+      else keyproj_bwd_combine_kernel<__nv_bfloat16, 1><<<grid, 256, 0, st>>>(a);
   }
   return cudaGetLastError();
 }

@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(VEC > 1 ? 256 : 1024) lrid_kernel(const __grid
                   dwp = fmaf(gp[c][e], Elem<T>::to_f(r[j][c].e[e]), dwp);
                   gvv[e] = w * gp[c][e];
                 }
-                store_pack<T, VEC>(sgv[s] + t * d + vh * dv + vidx * VEC, gvv);
+                if (sgv[s]) store_pack<T, VEC>(sgv[s] + t * d + vh * dv + vidx * VEC, gvv);
               }
             }
             dwp = group_sum(dwp, rg);
@@ -606,7 +606,7 @@ cudaError_t lrid_backward_launch(int dtype, const LridPlan& p, const LridIO& io,
   a.p = p;
   fill_tables(a, p, io.values, io.vstr, io.keys, io.kstr);
   for (int s = 0; s < p.S; ++s) {
-    a.gv[s] = gio.grad_values[s];
+    a.gv[s] = gio.grad_values ? gio.grad_values[s] : nullptr;
     a.gk[s] = gio.grad_keys[s];
   }
   a.qmode = io.qmode;

@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(288, 2) lrid_tma_kernel(const __grid_constant_
                 dwp = fmaf(gp[e], Elem<T>::to_f(r[j].e[e]), dwp);
                 gvv[e] = w * gp[e];
               }
-              store_pack<T, VEC>(sgv[s] + t * d + col, gvv);
+              if (sgv[s]) store_pack<T, VEC>(sgv[s] + t * d + col, gvv);
             }
             dwp = group_sum(dwp, rg);
             if ((vj & 31) == 0 && vh < H) sm_dwp[((slot * H + vh) * S + s) * wph + (vj >> 5)] = dwp;
@@ -720,7 +720,7 @@ cudaError_t lrid_tma_backward_launch(int dtype, const LridPlan& p, const TmaLayo
   LridArgs a{};
   fill_common(a, p, L, io);
   for (int s = 0; s < p.S; ++s) {
-    a.gv[s] = gio.grad_values[s];
+    a.gv[s] = gio.grad_values ? gio.grad_values[s] : nullptr;
     a.gk[s] = gio.grad_keys[s];
   }
   a.g = gio.grad_output;

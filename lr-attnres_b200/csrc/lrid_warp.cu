@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
                 dwp[s0 + jj] = fmaf(gp[e], Elem<T>::to_f(r4[jj].e[e]), dwp[s0 + jj]);
                 gv[e] = wgt * gp[e];
               }
-              store_pack<T, VEC>(sgv[s0 + jj] + t * d + col, gv);
+              if (sgv[s0 + jj]) store_pack<T, VEC>(sgv[s0 + jj] + t * d + col, gv);
             }
           }
         }
@@ -580,7 +580,7 @@ cudaError_t lrid_warp_backward_launch(int dtype, const LridPlan& p, const TmaLay
   LridArgs a{};
   fill_stream_common(a, p, L, io);
   for (int s = 0; s < p.S; ++s) {
-    a.gv[s] = gio.grad_values[s];
+    a.gv[s] = gio.grad_values ? gio.grad_values[s] : nullptr;
     a.gk[s] = gio.grad_keys[s];
   }
   a.g = gio.grad_output;

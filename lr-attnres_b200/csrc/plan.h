@@ -151,9 +151,10 @@ namespace attnres {
 cudaError_t keyproj_launch(int S, long long N, int d, int R, int dtype, const void* const* values,
                            const int64_t* vstr, const void* w, long long w_stride, int value_norm, float eps,
                            void* keys, float* inv_rms, bool allow_tc, cudaStream_t st, bool* used_tc);
-cudaError_t keyproj_bwd_combine_launch(int S, long long N, int d, int R, int dtype, const void* const* values,
-                                       const int64_t* vstr, void* const* grad_values, const void* dn,
-                                       const void* dk, const void* keys, const float* inv_rms, int value_norm,
-                                       cudaStream_t st);
+cudaError_t keyproj_bwd_combine_launch(int S, long long N, int d, int R, int H, int dtype,
+                                       const void* const* values, const int64_t* vstr,
+                                       void* const* grad_values, const void* dn, const void* dk,
+                                       const void* keys, const float* inv_rms, const void* g,
+                                       const float* alpha, int value_norm, cudaStream_t st);
 cudaError_t read_keyproj_status(unsigned* status, bool reset);
 }  // namespace attnres

@@ -22,13 +22,14 @@ def kernel_path(request, monkeypatch):
     assert _native.device_status(reset=True) == 0
 
 
-def run_kv(inp, B, T, H, scale, key_norm, dtype, value_norm=True):
+def run_kv(inp, B, T, H, scale, key_norm, dtype, value_norm=True, normalize_output=False):
     import attnres_b200 as A
 
     values = [dev_rows(v, B, T, dtype) for v in inp["values"]]
     w = torch.tensor(inp["key_weight"], device="cuda", dtype=torch.float32).to(dtype).requires_grad_(True)
     q = torch.tensor(inp["query"], device="cuda", dtype=torch.float32, requires_grad=True)
-    out = A.lrid_attention_residual_read_key_from_value(values, w, q, H, scale, key_norm, value_norm=value_norm)
+    out = A.lrid_attention_residual_read_key_from_value(values, w, q, H, scale, key_norm, value_norm=value_norm,
+                                                        normalize_output=normalize_output)
     out.backward(dev_rows(inp["grad_output"], B, T, dtype, requires_grad=False))
     torch.cuda.synchronize()
     return {"out": to_np(out).reshape(B * T, -1),
@@ -36,13 +37,16 @@ def run_kv(inp, B, T, H, scale, key_norm, dtype, value_norm=True):
             "dW": to_np(w.grad), "dq": to_np(q.grad).reshape(-1)}
 
 
-def oracle_kv(inp, H, scale, key_norm, dtype, value_norm=True):
+def oracle_kv(inp, H, scale, key_norm, dtype, value_norm=True, normalize_output=False):
     eps = float(torch.finfo(dtype).eps)
+    kw = {}
+    if normalize_output:
+        kw = dict(output_norm=oracle.NORM_PER_HEAD if H == 1 else oracle.NORM_ROW, output_eps=eps)
     v, w = rounded(inp["values"], dtype), rounded(inp["key_weight"], dtype)
     q = rounded(inp["query"], dtype)
     g = rounded(inp["grad_output"], dtype)
-    out = oracle.lrid_kv_forward(v, w, H, scale, key_norm, value_norm=value_norm, value_eps=eps, query=q)[0]
-    res = oracle.lrid_kv_backward(v, w, H, scale, key_norm, g, value_norm=value_norm, value_eps=eps, query=q)
+    out = oracle.lrid_kv_forward(v, w, H, scale, key_norm, value_norm=value_norm, value_eps=eps, query=q, **kw)[0]
+    res = oracle.lrid_kv_backward(v, w, H, scale, key_norm, g, value_norm=value_norm, value_eps=eps, query=q, **kw)
     res["out"] = out
     return res
 
@@ -102,3 +106,13 @@ def test_kv_read_bf16(S, N, D, R, H):
     res = run_kv(inp, 1, N, H, 1.0 / np.sqrt(R // H), True, torch.bfloat16)
     ref = oracle_kv(inp, H, 1.0 / np.sqrt(R // H), True, torch.bfloat16)
     compare(res, ref, torch.bfloat16, N)
+
+
+@pytest.mark.parametrize("H", [1, 2])
+def test_kv_read_output_norm_bf16(H):
+    """With the output normalised the read backward writes dV itself and the
+    projection backward adds into it (read-modify-write path)."""
+    inp = make(5, 150, 256, 64, H, seed=9 + H)
+    res = run_kv(inp, 1, 150, H, 0.25, True, torch.bfloat16, normalize_output=True)
+    ref = oracle_kv(inp, H, 0.25, True, torch.bfloat16, normalize_output=True)
+    compare(res, ref, torch.bfloat16, 150)
