@@ -82,9 +82,9 @@ bool values_vectorizable(int S, int esz, const void* const* values, const int64_
 }
 
 // Which LRID kernel family to use (ATTNRES_B200_PATH):
-//   auto (default) : the bulk-copy pipelines (forward: CTA-tile first, then
-//                    warp-per-token; backward: warp-per-token first), else
-//                    register streaming -- the first whose layout rules hold
+//   auto (default) : the streaming warp pipeline, else the CTA-tile
+//                    bulk-copy pipeline, else register streaming -- the first
+//                    whose layout rules hold
 //   tma            : skip the warp-per-token pipeline
 //   warp           : skip the CTA-tile pipeline
 //   simt           : register-streaming kernels only
@@ -187,12 +187,10 @@ int attnres_lrid_forward(int num_sources, int64_t num_tokens, int value_dim, int
   attnres::TmaLayout wl{}, tl{};
   attnres::LridPlan tplan{};
   int nw = 0;
-  // forward: the CTA-tile pipeline first (measured faster on B200 for the
-  // forward), then the warp-per-token pipeline
-  const bool tma = bulk && pc != PATH_WARP &&
-                   attnres::lrid_tma_plan(plan, esz, false, false, has_qd, &tplan, &tl);
-  const bool warp = bulk && !tma && pc != PATH_TMA &&
+  const bool warp = bulk && pc != PATH_TMA &&
                     attnres::lrid_warp_plan(plan, esz, false, false, has_qd, output_norm, &wl, &nw);
+  const bool tma = bulk && !warp && pc != PATH_WARP &&
+                   attnres::lrid_tma_plan(plan, esz, false, false, has_qd, &tplan, &tl);
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
   cudaError_t e = warp ? attnres::lrid_warp_forward_launch(dtype, plan, wl, nw, io, cs)
                   : tma ? attnres::lrid_tma_forward_launch(dtype, tplan, tl, io, cs)

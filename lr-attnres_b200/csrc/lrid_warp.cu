@@ -98,22 +98,26 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
 
   const T* gsrc = static_cast<const T*>(a.g);
   const T* qsrc = static_cast<const T*>(a.qdyn);
-  auto issue = [&](long long j) {  // lane 0 only
+  // Issue the copies of unit j: lane 0 posts the byte count, then lane i
+  // copies row i (the whole warp calls this, converged).
+  auto issue = [&](long long j) {
     const long long t = first + (j / U1) * step;
     const int u = static_cast<int>(j % U1);
     unsigned char* st = ring + static_cast<size_t>(j % NSW) * L.stage_bytes;
     uint64_t* bar = &wbars[j % NSW];
     if (u == 0) {
       const uint32_t kb = R * sizeof(T);
-      mbar_arrive_expect_tx(bar, S * kb + (has_qd ? kb : 0));
-      for (int s = 0; s < S; ++s) bulk_g2s(st + s * kb, sk[s] + t * sks[s], kb, bar);
-      if (has_qd) bulk_g2s(st + S * kb, qsrc + t * R, kb, bar);
+      if (lane == 0) mbar_arrive_expect_tx(bar, S * kb + (has_qd ? kb : 0));
+      __syncwarp();
+      for (int s = lane; s < S; s += 32) bulk_g2s(st + s * kb, sk[s] + t * sks[s], kb, bar);
+      if (has_qd && lane == (S & 31)) bulk_g2s(st + S * kb, qsrc + t * R, kb, bar);
     } else {
       const int c0 = (u - 1) * CW;
       const uint32_t cb = CW * sizeof(T);
-      mbar_arrive_expect_tx(bar, S * cb + (BWD ? cb : 0));
-      for (int s = 0; s < S; ++s) bulk_g2s(st + s * cb, sv[s] + t * svs[s] + c0, cb, bar);
-      if (BWD) bulk_g2s(st + S * cb, gsrc + t * d + c0, cb, bar);
+      if (lane == 0) mbar_arrive_expect_tx(bar, S * cb + (BWD ? cb : 0));
+      __syncwarp();
+      for (int s = lane; s < S; s += 32) bulk_g2s(st + s * cb, sv[s] + t * svs[s] + c0, cb, bar);
+      if (BWD && lane == (S & 31)) bulk_g2s(st + S * cb, gsrc + t * d + c0, cb, bar);
     }
   };
 
@@ -142,18 +146,15 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
 #pragma unroll
   for (int e = 0; e < KE; ++e) q[e] = qs[e];
 
-  if (lane == 0)
-    for (long long j = 0; j < J && j < NSW - 1; ++j) issue(j);
+  for (long long j = 0; j < J && j < NSW - 1; ++j) issue(j);
 
   long long j = 0;
   for (; j < J; ++j) {
     if (j + NSW - 1 < J) {
       // stage (j - 1) % NSW has been consumed by every lane: refill it
       __syncwarp();
-      if (lane == 0) {
-        fence_proxy_async_smem();
-        issue(j + NSW - 1);
-      }
+      fence_proxy_async_smem();
+      issue(j + NSW - 1);
     }
     if (!mbar_wait_bounded(&wbars[j % NSW], static_cast<uint32_t>((j / NSW) & 1))) {
       if (lane == 0) atomicOr(&g_warp_status, kStatusFullWaitTimeout);
