@@ -216,6 +216,31 @@ int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, in
                                          int value_norm, void* stream);
 
 /*
+ * Cached-logit block read ("phase 1"): Q reads of the same S sources whose
+ * logits were computed once. Replaces attention_residual_phase1_from_logits
+ * (attnres_ops.py:3910-3961) and its Triton kernels (:933-989, :1069-1140).
+ *   alpha = softmax over s of logits[q][:][n]; output[q][n] = sum_s alpha V_s[n]
+ *   lse[q][n] = logsumexp over s;  optional rms norm of each output row (ROW)
+ * logits: logit_dtype [Q][S][N] dense; output: dtype [Q][N][d] dense;
+ * lse, output_inv_rms: float [Q][N]. Q <= 16.
+ */
+int attnres_phase1_forward(int num_sources, int num_queries, int64_t num_tokens, int value_dim, int dtype,
+                           const void* const* values, const int64_t* value_row_strides, const void* logits,
+                           int logit_dtype, int output_norm, float output_eps, void* output, float* lse,
+                           float* output_inv_rms, void* stream);
+
+/*
+ * Phase-1 backward: grad_values[s] (dtype [N, d] dense) = sum_q alpha g'_q;
+ * grad_logits (logit_dtype [Q][S][N]) = alpha * (<g'_q, V_s> - sum_r alpha <g'_q, V_r>)
+ *                                       + grad_lse[q][n] * alpha   (grad_lse may be NULL).
+ */
+int attnres_phase1_backward(int num_sources, int num_queries, int64_t num_tokens, int value_dim, int dtype,
+                            const void* const* values, const int64_t* value_row_strides, const void* logits,
+                            int logit_dtype, int output_norm, float output_eps, const void* grad_output,
+                            const float* grad_lse, const void* normed_output, const float* output_inv_rms,
+                            void* const* grad_values, void* grad_logits, void* stream);
+
+/*
  * Base AttnRes read, forward (keys are the values themselves).
  * Replaces _attnres_read_list_triton (attnres_ops.py:2301) /
  * _attnres_list_read_kernel (attnres_ops.py:267).

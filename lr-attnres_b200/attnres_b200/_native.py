@@ -35,6 +35,8 @@ EXPORTED_SYMBOLS = (
     "attnres_lrid_backward_noalloc",
     "attnres_lrid_key_projection",
     "attnres_lrid_key_projection_backward",
+    "attnres_phase1_forward",
+    "attnres_phase1_backward",
     "attnres_noalloc_scratch_bytes",
 )
 
@@ -99,6 +101,10 @@ def load(path=None):
     L.attnres_lrid_key_projection.argtypes = [I, I64, I, I, I, PP, PI64, P, I64, I, F, P, P, P]
     L.attnres_lrid_key_projection_backward.restype = I
     L.attnres_lrid_key_projection_backward.argtypes = [I, I64, I, I, I, I, PP, PI64, PP, P, P, P, P, P, P, I, P]
+    L.attnres_phase1_forward.restype = I
+    L.attnres_phase1_forward.argtypes = [I, I, I64, I, I, PP, PI64, P, I, I, F, P, P, P, P]
+    L.attnres_phase1_backward.restype = I
+    L.attnres_phase1_backward.argtypes = [I, I, I64, I, I, PP, PI64, P, I, I, F, P, P, P, P, PP, P, P]
     L.attnres_base_forward.restype = I
     L.attnres_base_forward.argtypes = [
         I, I64, I, I, PP, PI64, P, I, F, P, I, F, P, P, P,

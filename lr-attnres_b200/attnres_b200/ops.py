@@ -911,3 +911,118 @@ def lrid_attention_residual_read_key_from_value(
     out, _, _, _, _ = lrid_kv_read(values, key_weight, q, g, qd, bias, int(num_heads), float(logit_scale),
                                    bool(key_norm), norm, bool(value_norm))
     return out
+
+
+# ---------------------------------------------------------------------------
+# attnres::phase1_from_logits — cached-logit block read (attnres_ops.py:3910)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("attnres::phase1_from_logits", mutates_args=())
+def phase1_from_logits(values: List[Tensor], logits: Tensor, normalize_output: bool) -> tuple[Tensor, Tensor, Tensor]:
+    """values: S sources [*lead, D]; logits [Q, S, *lead]. Returns
+    (out [Q, *lead, D], lse [Q, *lead] fp32, output_inv_rms [Q, N] or [1])."""
+    values = list(values)
+    S, d = len(values), values[0].size(-1)
+    if S < 1 or S > N.MAX_SOURCES:
+        raise RuntimeError(f"attnres_b200: phase1 needs 1..{N.MAX_SOURCES} sources")
+    Q = logits.size(0)
+    if logits.size(1) != S:
+        raise RuntimeError("attnres_b200: logits must be [Q, S, ...] with S = number of sources")
+    _require_cuda([*values, logits], "phase1 inputs")
+    dtype = values[0].dtype
+    rows, strides = _sources(values, d, dtype)
+    n = _ntok(values[0])
+    lead = _lead_shape(values[0])
+    lg = logits.reshape(Q, S, n).contiguous()
+    device = values[0].device
+    out = torch.empty((Q, *lead, d), device=device, dtype=dtype)
+    lse = torch.empty((Q, *lead), device=device, dtype=torch.float32)
+    inv = torch.empty((Q, n) if normalize_output else (1,), device=device, dtype=torch.float32)
+    with torch.cuda.device(device):
+        rc = N.load().attnres_phase1_forward(
+            S, Q, n, d, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            _ptr(lg), _dtype_code(lg.dtype), N.NORM_ROW if normalize_output else N.NORM_NONE,
+            float(torch.finfo(dtype).eps), _ptr(out), _ptr(lse), _ptr(inv) if normalize_output else None,
+            _stream_ptr(device))
+    N.check(rc, "attnres_phase1_forward")
+    return out, lse, inv
+
+
+@phase1_from_logits.register_fake
+def _(values, logits, normalize_output):
+    v0 = values[0]
+    n = v0.numel() // v0.size(-1)
+    Q = logits.size(0)
+    return (v0.new_empty((Q, *v0.shape)), v0.new_empty((Q, *v0.shape[:-1]), dtype=torch.float32),
+            v0.new_empty((Q, n) if normalize_output else (1,), dtype=torch.float32))
+
+
+@torch.library.custom_op("attnres::phase1_from_logits_backward", mutates_args=())
+def phase1_from_logits_backward(values: List[Tensor], logits: Tensor, grad_output: Tensor,
+                                grad_lse: Optional[Tensor], normed_output: Tensor, output_inv_rms: Tensor,
+                                normalize_output: bool) -> tuple[List[Tensor], Tensor]:
+    values = list(values)
+    S, d = len(values), values[0].size(-1)
+    Q = logits.size(0)
+    dtype = values[0].dtype
+    rows, strides = _sources(values, d, dtype)
+    n = _ntok(values[0])
+    lg = logits.reshape(Q, S, n).contiguous()
+    device = values[0].device
+    g = grad_output.to(dtype).reshape(Q, n, d).contiguous()
+    gl = None if grad_lse is None else grad_lse.to(torch.float32).reshape(Q, n).contiguous()
+    y = normed_output.to(dtype).reshape(Q, n, d).contiguous() if normalize_output else None
+    yi = output_inv_rms.contiguous() if normalize_output else None
+    gv = [torch.empty((*_lead_shape(v), d), device=device, dtype=dtype) for v in values]
+    dlg = torch.empty_like(lg)
+    with torch.cuda.device(device):
+        rc = N.load().attnres_phase1_backward(
+            S, Q, n, d, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            _ptr(lg), _dtype_code(lg.dtype), N.NORM_ROW if normalize_output else N.NORM_NONE,
+            float(torch.finfo(dtype).eps), _ptr(g), _ptr(gl), _ptr(y), _ptr(yi),
+            N.ptr_array([t.data_ptr() for t in gv]), _ptr(dlg), _stream_ptr(device))
+    N.check(rc, "attnres_phase1_backward")
+    return gv, dlg.reshape(logits.shape)
+
+
+@phase1_from_logits_backward.register_fake
+def _(values, logits, grad_output, grad_lse, normed_output, output_inv_rms, normalize_output):
+    return [v.new_empty(v.shape) for v in values], logits.new_empty(logits.shape)
+
+
+def _phase1_setup(ctx, inputs, output):
+    values, logits, normalize_output = inputs
+    out, lse, inv = output
+    ctx.save_for_backward(logits, out, inv, *values)
+    ctx.normalize_output = bool(normalize_output)
+
+
+def _phase1_bwd(ctx, grad_out, grad_lse, grad_inv):
+    logits, out, inv, *values = ctx.saved_tensors
+    gv, dlg = phase1_from_logits_backward(list(values), logits, grad_out, grad_lse, out, inv, ctx.normalize_output)
+    return gv, dlg, None
+
+
+phase1_from_logits.register_autograd(_phase1_bwd, setup_context=_phase1_setup)
+
+
+def attention_residual_phase1_from_logits(values, logits: Tensor, force_triton: bool = False,
+                                          normalize_output: bool = False):
+    """Cached-logit block read (reference attnres_ops.py:3910): values are S
+    sources (list or stacked [S, ...]), logits [Q, S, ...]. Returns
+    (out [Q, ..., D], lse [Q, ...] fp32)."""
+    values = _as_list(values)
+    if len(values) == 0:
+        raise RuntimeError("Cached-logit AttnRes phase1 requires at least one source")
+    out, lse, _ = phase1_from_logits(values, logits, bool(normalize_output))
+    return out, lse
+
+
+def attention_residual_average_read(values, normalize_output: bool = False, force_triton: bool = False) -> Tensor:
+    """Mean over the sources (reference attnres_ops.py:2568): the base read with
+    a zero query and no key norm gives every source the weight 1/S."""
+    values = _as_list(values)
+    if len(values) == 1:
+        return _norm(values[0]) if normalize_output else values[0]
+    q = torch.zeros(values[0].size(-1), device=values[0].device, dtype=values[0].dtype)
+    out, _ = base_read(values, q, None, False, bool(normalize_output))
+    return out

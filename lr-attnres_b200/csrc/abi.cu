@@ -469,4 +469,60 @@ int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, in
   return ATTNRES_OK;
 }
 
+int attnres_phase1_forward(int num_sources, int num_queries, int64_t num_tokens, int value_dim, int dtype,
+                           const void* const* values, const int64_t* value_row_strides, const void* logits,
+                           int logit_dtype, int output_norm, float output_eps, void* output, float* lse,
+                           float* output_inv_rms, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, 0, 1, dtype, values, value_row_strides, nullptr,
+                         nullptr, false);
+  if (rc) return rc;
+  if (num_queries < 1 || num_queries > 16)
+    return fail(ATTNRES_ERR_UNSUPPORTED, "num_queries=%d outside [1, 16]", num_queries);
+  if (elem_size(logit_dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown logit dtype %d", logit_dtype);
+  if ((rc = check_norm(output_norm, false))) return rc;
+  if (num_tokens > 0 && (!logits || !output || !lse))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase1 forward: NULL logits/output/lse");
+  if (num_tokens == 0) return ATTNRES_OK;
+  const void* extra[1] = {output};
+  const bool vec = values_vectorizable(num_sources, elem_size(dtype), values, value_row_strides, extra, 1);
+  cudaError_t e = attnres::phase1_launch(dtype, logit_dtype, num_sources, num_queries, num_tokens, value_dim, vec,
+                                         values, value_row_strides, logits, output_norm != ATTNRES_NORM_NONE,
+                                         output_eps, output, lse, output_inv_rms, nullptr, nullptr, nullptr,
+                                         nullptr, nullptr, nullptr, false, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_phase1_forward launch");
+  return ATTNRES_OK;
+}
+
+int attnres_phase1_backward(int num_sources, int num_queries, int64_t num_tokens, int value_dim, int dtype,
+                            const void* const* values, const int64_t* value_row_strides, const void* logits,
+                            int logit_dtype, int output_norm, float output_eps, const void* grad_output,
+                            const float* grad_lse, const void* normed_output, const float* output_inv_rms,
+                            void* const* grad_values, void* grad_logits, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, 0, 1, dtype, values, value_row_strides, nullptr,
+                         nullptr, false);
+  if (rc) return rc;
+  if (num_queries < 1 || num_queries > 16)
+    return fail(ATTNRES_ERR_UNSUPPORTED, "num_queries=%d outside [1, 16]", num_queries);
+  if (elem_size(logit_dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown logit dtype %d", logit_dtype);
+  if ((rc = check_norm(output_norm, false))) return rc;
+  if (num_tokens == 0) return ATTNRES_OK;
+  if (!logits || !grad_output || !grad_values || !grad_logits)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase1 backward: NULL buffer");
+  if (output_norm != ATTNRES_NORM_NONE && (!normed_output || !output_inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase1 backward with output norm needs normed_output/output_inv_rms");
+  const void* extra[2 + ATTNRES_MAX_SOURCES];
+  int n_extra = 0;
+  extra[n_extra++] = grad_output;
+  extra[n_extra++] = output_norm != ATTNRES_NORM_NONE ? normed_output : nullptr;
+  for (int s = 0; s < num_sources; ++s) extra[n_extra++] = grad_values[s];
+  const bool vec = values_vectorizable(num_sources, elem_size(dtype), values, value_row_strides, extra, n_extra);
+  cudaError_t e = attnres::phase1_launch(dtype, logit_dtype, num_sources, num_queries, num_tokens, value_dim, vec,
+                                         values, value_row_strides, logits, output_norm != ATTNRES_NORM_NONE,
+                                         output_eps, nullptr, nullptr, nullptr, grad_output, normed_output,
+                                         output_inv_rms, grad_lse, grad_values, grad_logits, true,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_phase1_backward launch");
+  return ATTNRES_OK;
+}
+
 }  // extern "C"

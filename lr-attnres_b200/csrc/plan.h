@@ -158,3 +158,12 @@ cudaError_t keyproj_bwd_combine_launch(int S, long long N, int d, int R, int H, 
                                        const float* alpha, int value_norm, cudaStream_t st);
 cudaError_t read_keyproj_status(unsigned* status, bool reset);
 }  // namespace attnres
+
+namespace attnres {
+// Cached-logit multi-query read (phase1.cu).
+cudaError_t phase1_launch(int dtype, int logit_dtype, int S, int Q, long long N, int d, bool full_vec,
+                          const void* const* values, const int64_t* vstr, const void* logits, int out_norm,
+                          float out_eps, void* out, float* lse, float* out_inv, const void* g, const void* y,
+                          const float* y_inv, const float* glse, void* const* grad_values, void* dlogits,
+                          bool bwd, cudaStream_t st);
+}  // namespace attnres

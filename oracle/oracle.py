@@ -183,3 +183,40 @@ def lrid_kv_backward(values, weight, num_heads, logit_scale, key_norm, grad_outp
     res["dW"] = np.einsum("snr,snd->rd", dk, nhat)
     res["keys"] = keys
     return res
+
+
+def phase1_forward(values, logits, normalize_output=False, output_eps=float(np.finfo(np.float32).eps)):
+    """Cached-logit read, double precision (attnres_ops.py:3955-3961):
+    values [S, N, d], logits [Q, S, N] -> out [Q, N, d], lse [Q, N]."""
+    v = np.asarray(values, np.float64)
+    lg = np.asarray(logits, np.float64)
+    m = lg.max(axis=1, keepdims=True)
+    e = np.exp(lg - m)
+    alpha = e / e.sum(axis=1, keepdims=True)  # [Q, S, N]
+    acc = np.einsum("qsn,snd->qnd", alpha, v)
+    lse = (m[:, 0] + np.log(e.sum(axis=1)))
+    inv = None
+    if normalize_output:
+        inv = 1.0 / np.sqrt((acc * acc).mean(-1, keepdims=True) + output_eps)
+        out = acc * inv
+    else:
+        out = acc
+    return out, lse, alpha, acc, inv
+
+
+def phase1_backward(values, logits, grad_output, grad_lse=None, normalize_output=False,
+                    output_eps=float(np.finfo(np.float32).eps)):
+    """Analytic gradients of phase1_forward (as the reference's backward
+    kernels compute them, attnres_ops.py:1069-1140)."""
+    v = np.asarray(values, np.float64)
+    out, lse, alpha, acc, inv = phase1_forward(values, logits, normalize_output, output_eps)
+    g = np.asarray(grad_output, np.float64)
+    if normalize_output:
+        y = acc * inv
+        g = inv * (g - y * (g * y).mean(-1, keepdims=True))
+    dV = np.einsum("qsn,qnd->snd", alpha, g)
+    dw = np.einsum("qnd,snd->qsn", g, v)
+    dl = alpha * (dw - (alpha * dw).sum(axis=1, keepdims=True))
+    if grad_lse is not None:
+        dl = dl + np.asarray(grad_lse, np.float64)[:, None, :] * alpha
+    return {"dV": dV, "dlogits": dl}

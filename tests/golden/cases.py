@@ -38,6 +38,9 @@ CASES = [
          key_norm=True, query="static", seed=31),
     dict(name="lrid_kv_h1_nonorm", kind="lrid_kv", S=4, B=1, T=6, D=64, R=16, H=1, scale=0.25,
          key_norm=True, query="static", value_norm=False, seed=32),
+    # cached-logit block read (attention_residual_phase1_from_logits, attnres_ops.py:3910)
+    dict(name="phase1_q3", kind="phase1", S=5, Q=3, B=2, T=6, D=64, seed=41),
+    dict(name="phase1_q2_norm", kind="phase1", S=4, Q=2, B=1, T=9, D=32, normalize_output=True, seed=42),
     # base AttnRes read, mirrors test_fused_base_attnres_matches_torch (:884-895)
     dict(name="base_small_kn", kind="base", S=5, B=2, T=5, D=64, key_norm=True, seed=21),
     dict(name="base_small_nokn", kind="base", S=5, B=2, T=5, D=64, key_norm=False, seed=22),
@@ -60,6 +63,11 @@ def case_inputs(case):
         inp["query"] = f(H, R // H)
         inp["query_dynamic"] = f(N, H, R // H)
         inp["gate"] = (0.1 + 0.2 * rng.standard_normal(H)).astype(np.float32)
+    elif case["kind"] == "phase1":
+        inp["logits"] = f(case["Q"], S, N)
+        inp["grad_lse"] = f(case["Q"], N)
+        inp["grad_output"] = f(case["Q"], N, D)
+        return inp
     else:
         inp["query"] = (f(D) * np.float32(case.get("query_std", 1.0))).astype(np.float32)
     if case["kind"] == "lrid_kv":

@@ -41,8 +41,22 @@ def run_case(ref, case):
     B, T = case["B"], case["T"]
     t = lambda x: torch.tensor(x, dtype=torch.float32, requires_grad=True)  # noqa: E731
     values = [t(v.reshape(B, T, -1)) for v in inp["values"]]
-    grad_out = torch.tensor(inp["grad_output"].reshape(B, T, -1), dtype=torch.float32)
+    grad_out = (torch.tensor(inp["grad_output"].reshape(B, T, -1), dtype=torch.float32)
+                if kind != "phase1" else None)
     res = {}
+    if kind == "phase1":
+        Q = case["Q"]
+        vs = torch.tensor(inp["values"].reshape(-1, B, T, inp["values"].shape[-1]), requires_grad=True)
+        lg = torch.tensor(inp["logits"].reshape(Q, -1, B, T), requires_grad=True)
+        out, lse = ref.attention_residual_phase1_from_logits(
+            vs, lg, normalize_output=case.get("normalize_output", False))
+        (out * torch.tensor(inp["grad_output"].reshape(Q, B, T, -1))).sum().add_(
+            (lse * torch.tensor(inp["grad_lse"].reshape(Q, B, T))).sum()).backward()
+        res["out"] = out.detach().numpy().reshape(Q, B * T, -1)
+        res["lse"] = lse.detach().numpy().reshape(Q, B * T)
+        res["dV"] = vs.grad.numpy().reshape(vs.shape[0], B * T, -1)
+        res["dlogits"] = lg.grad.numpy().reshape(Q, -1, B * T)
+        return res
     if kind == "lrid_kv":
         # keys from the values exactly as model.py:344-356 composes them
         import torch.nn.functional as F

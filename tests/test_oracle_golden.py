@@ -19,12 +19,18 @@ F32_EPS = float(np.finfo(np.float32).eps)
 def oracle_case(case):
     inp = case_inputs(case)
     norm = oracle.NORM_NONE
-    if case.get("normalize_output"):
+    if case.get("normalize_output") and case["kind"] != "phase1":
         if case["kind"] == "base":
             norm = oracle.NORM_ROW
         else:
             norm = oracle.NORM_PER_HEAD if case["H"] == 1 else oracle.NORM_ROW
     bias = inp["logit_bias"] if case.get("bias") else None
+    if case["kind"] == "phase1":
+        nrm = case.get("normalize_output", False)
+        out, lse, _, _, _ = oracle.phase1_forward(inp["values"], inp["logits"], nrm)
+        grads = oracle.phase1_backward(inp["values"], inp["logits"], inp["grad_output"], inp["grad_lse"], nrm)
+        grads["lse"] = lse
+        return out, grads
     if case["kind"] == "lrid_kv":
         vn = case.get("value_norm", True)
         args = (inp["values"], inp["key_weight"], case["H"], case["scale"], case["key_norm"])
@@ -70,6 +76,9 @@ def test_oracle_matches_reference_golden(case):
                 _close(name + "_sum", got.sum(axis=(1, 2)), gold[name + "_sum"], scale=10.0)
                 got = got[:, :keep]
             _close(name, got, gold[name])
+    for name in ("lse", "dlogits"):
+        if name in gold:
+            _close(name, grads[name], gold[name])
     if "dW" in gold:
         _close("dW", grads["dW"], gold["dW"], scale=4.0)
     for name in ("dq", "dgate", "dq_dynamic", "dbias"):
