@@ -1,0 +1,37 @@
+"""Every attnres:: operator has a fake (meta) implementation, so graphs that
+contain it can be traced (torch.compile / export) without running CUDA: the
+reference registers its ops for the same reason (attnres_ops.py:4632)."""
+import torch
+from torch._subclasses.fake_tensor import FakeTensorMode
+
+import attnres_b200  # noqa: F401  (registers torch.ops.attnres.*)
+
+
+def _fake(mode, *shape, dtype=torch.bfloat16):
+    with mode:
+        return torch.empty(*shape, dtype=dtype, device="cuda")
+
+
+def test_fake_shapes_of_all_ops():
+    mode = FakeTensorMode(allow_non_fake_inputs=False)
+    S, B, T, D, R, H, Q = 5, 2, 7, 64, 16, 2, 3
+    v = [_fake(mode, B, T, D) for _ in range(S)]
+    k = [_fake(mode, B, T, R) for _ in range(S)]
+    q = _fake(mode, H, R // H)
+    g = _fake(mode, B, T, D)
+    ops = torch.ops.attnres
+    with mode:
+        out, inv, alpha, kinv = ops.lrid_read_list(v, k, q, H, 0.5, True, False, True)
+        assert out.shape == (B, T, D) and alpha.shape == (B * T, H, S)
+        gv, gk, dq = ops.lrid_read_list_backward(v, k, q, g, out, inv, alpha, kinv, H, 0.5, True, False, True)
+        assert len(gv) == S and gk[0].shape == (B, T, R) and dq.shape == q.shape
+        out2, inv2 = ops.lrid_read(v, k, q, None, None, None, H, 0.5, True, 2)
+        assert inv2.shape == (B * T,)
+        w = _fake(mode, R, D)
+        o, oi, keys, vinv, al = ops.lrid_kv_read(v, w, q, None, None, None, H, 0.5, True, 0, True)
+        assert keys.shape == (S, B, T, R) and vinv.shape == (S, B * T) and al.shape == (B * T, H, S)
+        lg = _fake(mode, Q, S, B, T, dtype=torch.float32)
+        po, lse, pinv = ops.phase1_from_logits(v, lg, False)
+        assert po.shape == (Q, B, T, D) and lse.shape == (Q, B, T)
+        bo, binv = ops.base_read(v, _fake(mode, D), None, True, True)
+        assert bo.shape == (B, T, D) and binv.shape == (B * T,)
