@@ -98,21 +98,38 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
 
   const T* gsrc = static_cast<const T*>(a.g);
   const T* qsrc = static_cast<const T*>(a.qdyn);
-  // Issue the copies of unit j: lane 0 posts the byte count, then lane i
-  // copies row i (the whole warp calls this, converged).
-  auto issue = [&](long long j) {
-    const long long t = first + (j / U1) * step;
-    const int u = static_cast<int>(j % U1);
-    unsigned char* st = ring + static_cast<size_t>(j % NSW) * L.stage_bytes;
-    uint64_t* bar = &wbars[j % NSW];
-    if (u == 0) {
+  // Position of a unit in this warp's sequence, advanced incrementally (no
+  // division in the token loop): token row t, unit u within the token, ring
+  // stage st and the stage's phase parity ph.
+  struct Cursor {
+    long long t;
+    int u, st;
+    uint32_t ph;
+  };
+  auto advance = [&](Cursor& c) {
+    if (++c.u == U1) {
+      c.u = 0;
+      c.t += step;
+    }
+    if (++c.st == NSW) {
+      c.st = 0;
+      c.ph ^= 1u;
+    }
+  };
+  // Issue the copies of the unit at cursor c: lane 0 posts the byte count,
+  // then lane i copies row i (the whole warp calls this, converged).
+  auto issue = [&](const Cursor& c) {
+    const long long t = c.t;
+    unsigned char* st = ring + static_cast<size_t>(c.st) * L.stage_bytes;
+    uint64_t* bar = &wbars[c.st];
+    if (c.u == 0) {
       const uint32_t kb = R * sizeof(T);
       if (lane == 0) mbar_arrive_expect_tx(bar, S * kb + (has_qd ? kb : 0));
       __syncwarp();
       for (int s = lane; s < S; s += 32) bulk_g2s(st + s * kb, sk[s] + t * sks[s], kb, bar);
       if (has_qd && lane == (S & 31)) bulk_g2s(st + S * kb, qsrc + t * R, kb, bar);
     } else {
-      const int c0 = (u - 1) * CW;
+      const int c0 = (c.u - 1) * CW;
       const uint32_t cb = CW * sizeof(T);
       if (lane == 0) mbar_arrive_expect_tx(bar, S * cb + (BWD ? cb : 0));
       __syncwarp();
@@ -124,7 +141,8 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
   // key-segment mapping: groups of KL lanes, fixed head per lane
   const int G = 32 / KL;
   const int gidx = lane / KL, kl = lane % KL;
-  const int kh = gidx % H;
+  const int hshift = __ffs(H) - 1;  // H is a power of two
+  const int kh = gidx & (H - 1);
   const int kcol = kh * dk + kl * KE;
   const int rounds = (SH + G - 1) / G;
 
@@ -146,23 +164,32 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
 #pragma unroll
   for (int e = 0; e < KE; ++e) q[e] = qs[e];
 
-  for (long long j = 0; j < J && j < NSW - 1; ++j) issue(j);
+  Cursor pc{first, 0, 0, 0u};  // next unit to issue
+  long long issued = 0;
+  for (; issued < J && issued < NSW - 1; ++issued) {
+    issue(pc);
+    advance(pc);
+  }
 
+  Cursor cc{first, 0, 0, 0u};  // unit being consumed
   long long j = 0;
-  for (; j < J; ++j) {
-    if (j + NSW - 1 < J) {
-      // stage (j - 1) % NSW has been consumed by every lane: refill it
+  int hcnt = 0, hcur = 0;       // chunk position inside the current head
+  for (; j < J; ++j, advance(cc)) {
+    if (issued < J) {
+      // the stage of unit j - 1 has been consumed by every lane: refill it
       __syncwarp();
       fence_proxy_async_smem();
-      issue(j + NSW - 1);
+      issue(pc);
+      advance(pc);
+      ++issued;
     }
-    if (!mbar_wait_bounded(&wbars[j % NSW], static_cast<uint32_t>((j / NSW) & 1))) {
+    if (!mbar_wait_bounded(&wbars[cc.st], cc.ph)) {
       if (lane == 0) atomicOr(&g_warp_status, kStatusFullWaitTimeout);
       break;
     }
-    const unsigned char* st = ring + static_cast<size_t>(j % NSW) * L.stage_bytes;
-    const long long t = first + (j / U1) * step;
-    const int u = static_cast<int>(j % U1);
+    const unsigned char* st = ring + static_cast<size_t>(cc.st) * L.stage_bytes;
+    const long long t = cc.t;
+    const int u = cc.u;
 
     if (u == 0) {
       // ---- new token: key rows, logits, softmax ---------------------------
@@ -187,7 +214,7 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
       }
       for (int r = 0; r < rounds; ++r) {
         const int seg = r * G + gidx;  // seg = s * H + h, h == kh
-        const int s = seg / H;
+        const int s = seg >> hshift;
         float ss = 0.f, dot = 0.f;
         if (seg < SH) {
 #pragma unroll
@@ -239,7 +266,8 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
 
     // ---- value chunk c of this token ----------------------------------------
     const int c = u - 1;
-    const int h = c / cph;
+    if (c == 0) hcnt = hcur = 0;
+    const int h = hcur;
     const int col = c * CW + lane * VEC;
     const T* vt = reinterpret_cast<const T*>(st) + lane * VEC;  // + s * CW
     const float* al = sm_alpha + h * S;
@@ -266,6 +294,10 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
         for (int e = 0; e < VEC; ++e) acc[e] = fmaf(wgt, Elem<T>::to_f(r1.e[e]), acc[e]);
       }
       store_pack<T, VEC>(static_cast<T*>(a.out) + t * d + col, acc);
+      if (++hcnt == cph) {
+        hcnt = 0;
+        ++hcur;
+      }
     } else {
       float gp[VEC];
       {
@@ -295,7 +327,8 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
           }
         }
       }
-      if ((c + 1) % cph == 0) {
+      if (++hcnt == cph) {
+        hcnt = 0;
         // last chunk of head h: finish dw_s = <g', V_s> over the head
 #pragma unroll
         for (int s = 0; s < SMAX; ++s) {
@@ -305,6 +338,7 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
           }
           dwp[s] = 0.f;
         }
+        ++hcur;
       }
       if (u == C) {
         __syncwarp();
@@ -328,7 +362,7 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
         for (int e = 0; e < KE; ++e) dqt[e] = 0.f;
         for (int r = 0; r < rounds; ++r) {
           const int seg = r * G + gidx;
-          const int s = seg / H;
+          const int s = seg >> hshift;
           if (seg < SH) {
             const float c1 = sm_logit[kh * S + s] * a.scale;
             const float kinv = sm_kinv[kh * S + s];
@@ -390,9 +424,8 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
 
   if (j < J) {
     // gave up: let this warp's copies that are still in flight land first
-    const long long issued = (j + NSW - 1 < J) ? j + NSW - 1 : J;
-    for (long long i = j; i < issued; ++i)
-      if (!mbar_wait_bounded(&wbars[i % NSW], static_cast<uint32_t>((i / NSW) & 1)))
+    for (long long i = j; i < issued; ++i, advance(cc))
+      if (!mbar_wait_bounded(&wbars[cc.st], cc.ph))
         if (lane == 0) atomicOr(&g_warp_status, kStatusDrainTimeout);
   }
 
