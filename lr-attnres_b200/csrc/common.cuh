@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/attnres_b200.h"
 
 namespace attnres {
@@ -78,6 +80,71 @@ __device__ __forceinline__ void store_pack(T* p, const float (&x)[VEC]) {
 #pragma unroll
   for (int i = 0; i < VEC; ++i) r.e[i] = Elem<T>::from_f(x[i]);
   *reinterpret_cast<Pack<T, VEC>*>(p) = r;
+}
+
+// acc[e] = fma(w, x[e], acc[e]) over one pack, two lanes per instruction with
+// sm_100's packed fp32 FMA (each lane rounds exactly like fmaf). bf16 halves
+// widen to fp32 by a shift / mask of their 32-bit word.
+__device__ __forceinline__ void fma2(float& a0, float& a1, float w, float x0, float x1) {
+  asm("{\n\t.reg .b64 xa, wa, aa;\n\t"
+      "mov.b64 xa, {%2, %3};\n\tmov.b64 wa, {%4, %4};\n\tmov.b64 aa, {%0, %1};\n\t"
+      "fma.rn.f32x2 aa, wa, xa, aa;\n\tmov.b64 {%0, %1}, aa;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(x0), "f"(x1), "f"(w));
+}
+
+template <typename T, int VEC> __device__ __forceinline__ void unpack2(const Pack<T, VEC>&, int, float&, float&);
+
+template <typename T, int VEC>
+__device__ __forceinline__ void axpy_pack(float (&acc)[VEC], float w, const Pack<T, VEC>& x) {
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) {
+    float x0, x1;
+    unpack2<T, VEC>(x, i, x0, x1);
+    fma2(acc[2 * i], acc[2 * i + 1], w, x0, x1);
+  }
+}
+
+__device__ __forceinline__ void mul2(float& y0, float& y1, float w, float x0, float x1) {
+  asm("{\n\t.reg .b64 xa, wa, ya;\n\t"
+      "mov.b64 xa, {%2, %3};\n\tmov.b64 wa, {%4, %4};\n\t"
+      "mul.rn.f32x2 ya, wa, xa;\n\tmov.b64 {%0, %1}, ya;\n\t}"
+      : "=f"(y0), "=f"(y1)
+      : "f"(x0), "f"(x1), "f"(w));
+}
+
+__device__ __forceinline__ void fma2v(float& a0, float& a1, float g0, float g1, float x0, float x1) {
+  asm("{\n\t.reg .b64 xa, ga, aa;\n\t"
+      "mov.b64 xa, {%2, %3};\n\tmov.b64 ga, {%4, %5};\n\tmov.b64 aa, {%0, %1};\n\t"
+      "fma.rn.f32x2 aa, ga, xa, aa;\n\tmov.b64 {%0, %1}, aa;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(x0), "f"(x1), "f"(g0), "f"(g1));
+}
+
+// Widen element pair i of a pack to fp32.
+template <typename T, int VEC>
+__device__ __forceinline__ void unpack2(const Pack<T, VEC>& x, int i, float& x0, float& x1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const uint32_t u = reinterpret_cast<const uint32_t*>(x.e)[i];
+    x0 = __uint_as_float(u << 16);
+    x1 = __uint_as_float(u & 0xffff0000u);
+  } else {
+    x0 = Elem<T>::to_f(x.e[2 * i]);
+    x1 = Elem<T>::to_f(x.e[2 * i + 1]);
+  }
+}
+
+// acc + sum_e g[e] * x[e], even and odd elements in two packed chains.
+template <typename T, int VEC>
+__device__ __forceinline__ float dot_pack(float acc, const float (&g)[VEC], const Pack<T, VEC>& x) {
+  float a0 = acc, a1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) {
+    float x0, x1;
+    unpack2<T, VEC>(x, i, x0, x1);
+    fma2v(a0, a1, g[2 * i], g[2 * i + 1], x0, x1);
+  }
+  return a0 + a1;
 }
 
 template <typename T>

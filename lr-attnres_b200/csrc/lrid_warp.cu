@@ -275,23 +275,17 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
       float acc[VEC];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
-      int s = 0;
-      for (; s + 4 <= S; s += 4) {
-        Pack<T, VEC> r4[4];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) r4[jj] = lds_pack<T, VEC>(vt + (s + jj) * CW);
+      for (int s0 = 0; s0 < SMAX; s0 += 4) {
+        if (s0 < S) {
+          Pack<T, VEC> r4[4];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const float wgt = al[s + jj];
+          for (int jj = 0; jj < 4; ++jj)
+            if (s0 + jj < S) r4[jj] = lds_pack<T, VEC>(vt + (s0 + jj) * CW);
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) acc[e] = fmaf(wgt, Elem<T>::to_f(r4[jj].e[e]), acc[e]);
+          for (int jj = 0; jj < 4; ++jj)
+            if (s0 + jj < S) axpy_pack<T, VEC>(acc, al[s0 + jj], r4[jj]);
         }
-      }
-      for (; s < S; ++s) {
-        const Pack<T, VEC> r1 = lds_pack<T, VEC>(vt + s * CW);
-        const float wgt = al[s];
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[e] = fmaf(wgt, Elem<T>::to_f(r1.e[e]), acc[e]);
       }
       store_pack<T, VEC>(static_cast<T*>(a.out) + t * d + col, acc);
       if (++hcnt == cph) {
@@ -316,13 +310,13 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
           for (int jj = 0; jj < 4; ++jj) {
             if (s0 + jj < S) {
               const float wgt = al[s0 + jj];
-              float gv[VEC];
+              dwp[s0 + jj] = dot_pack<T, VEC>(dwp[s0 + jj], gp, r4[jj]);
+              if (sgv[s0 + jj]) {
+                float gv[VEC];
 #pragma unroll
-              for (int e = 0; e < VEC; ++e) {
-                dwp[s0 + jj] = fmaf(gp[e], Elem<T>::to_f(r4[jj].e[e]), dwp[s0 + jj]);
-                gv[e] = wgt * gp[e];
+                for (int e = 0; e < VEC; e += 2) mul2(gv[e], gv[e + 1], wgt, gp[e], gp[e + 1]);
+                store_pack<T, VEC>(sgv[s0 + jj] + t * d + col, gv);
               }
-              if (sgv[s0 + jj]) store_pack<T, VEC>(sgv[s0 + jj] + t * d + col, gv);
             }
           }
         }

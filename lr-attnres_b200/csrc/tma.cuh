@@ -19,6 +19,10 @@ enum DeviceStatusBits : unsigned {
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+// Longest time one try_wait may park the thread in hardware before it returns
+// false. Parked threads issue nothing, so a waiting warp leaves the issue slots
+// to the warps that have data; the bounded loop still checks the 2 s limit.
+constexpr uint32_t kSuspendHintNs = 1000000u;  // 1 ms
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -52,10 +56,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
