@@ -37,6 +37,9 @@ struct LridArgs {
   float* partials;
   int part_stride;
   int want_bias_grad;
+  // Streaming kernels: {next token, finished warps} counter pair for the
+  // dynamic token schedule; null selects the static round-robin schedule.
+  unsigned long long* claim;
   TmaLayout tma;
 };
 

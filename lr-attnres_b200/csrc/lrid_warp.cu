@@ -21,6 +21,9 @@
 // unambiguous. Waits are bounded (~2 s) and report through a status word.
 // Row widths must split into 512-byte chunks per head: (d/H) % (32*VEC) == 0.
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
 
 #include "lrid_args.cuh"
 #include "tma.cuh"
@@ -53,7 +56,8 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
   const int C = d / CW, cph = dv / CW, U1 = C + 1;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);  // [NW][NSW]
-  const T** sv = reinterpret_cast<const T**>(bars + kStreamMaxWarps * kStreamMaxStages);
+  long long* tokq_all = reinterpret_cast<long long*>(bars + kStreamMaxWarps * kStreamMaxStages);  // [NW][NSW]
+  const T** sv = reinterpret_cast<const T**>(tokq_all + kStreamMaxWarps * kStreamMaxStages);
   const T** sk = sv + S;
   long long* svs = reinterpret_cast<long long*>(sk + S);
   long long* sks = svs + S;
@@ -90,11 +94,26 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
   unsigned char* ring = stage0 + static_cast<size_t>(w) * NSW * L.stage_bytes;
   uint64_t* wbars = bars + w * NSW;
 
-  // tokens of this warp
-  const long long first = blockIdx.x + static_cast<long long>(w) * gridDim.x;
+  // Token schedule. Static: this warp takes tokens first, first + step, ...
+  // Dynamic (a.claim set): the warp takes the next unclaimed token from a
+  // global counter each time its copy issue reaches a new token, so warps on
+  // faster SMs take more tokens and all warps finish within about one token.
+  const long long N = P.N;
   const long long step = static_cast<long long>(NW) * gridDim.x;
-  const long long ntok = (P.N > first) ? (P.N - first + step - 1) / step : 0;
-  const long long J = ntok * U1;
+  long long stat_next = blockIdx.x + static_cast<long long>(w) * gridDim.x;
+  unsigned long long* claim = a.claim;
+  auto next_token = [&]() -> long long {
+    if (claim != nullptr) {
+      unsigned long long v = 0;
+      if (lane == 0) v = atomicAdd(claim, 1ull);
+      return static_cast<long long>(__shfl_sync(0xffffffffu, v, 0));
+    }
+    const long long t = stat_next;
+    stat_next += step;
+    return t;
+  };
+  // token of the key unit held in each ring stage (N marks the end)
+  long long* tokq = tokq_all + w * NSW;
 
   const T* gsrc = static_cast<const T*>(a.g);
   const T* qsrc = static_cast<const T*>(a.qdyn);
@@ -107,10 +126,7 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
     uint32_t ph;
   };
   auto advance = [&](Cursor& c) {
-    if (++c.u == U1) {
-      c.u = 0;
-      c.t += step;
-    }
+    if (++c.u == U1) c.u = 0;
     if (++c.st == NSW) {
       c.st = 0;
       c.ph ^= 1u;
@@ -164,24 +180,39 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
 #pragma unroll
   for (int e = 0; e < KE; ++e) q[e] = qs[e];
 
-  Cursor pc{first, 0, 0, 0u};  // next unit to issue
+  // Copy issue runs NSW - 1 units ahead of the consumer. Reaching a new token,
+  // it records the token in the stage's slot; a token >= N ends the issue.
+  Cursor pc{next_token(), 0, 0, 0u};  // next unit to issue
+  bool issuing = true;
   long long issued = 0;
-  for (; issued < J && issued < NSW - 1; ++issued) {
+  auto issue_next = [&]() {
+    if (pc.u == 0) {
+      tokq[pc.st] = pc.t;  // every lane writes the same value
+      if (pc.t >= N) {
+        issuing = false;
+        return;
+      }
+    }
     issue(pc);
+    ++issued;
     advance(pc);
-  }
+    if (pc.u == 0) pc.t = next_token();
+  };
+  for (int i = 0; i < NSW - 1 && issuing; ++i) issue_next();
 
-  Cursor cc{first, 0, 0, 0u};  // unit being consumed
+  Cursor cc{0, 0, 0, 0u};  // unit being consumed
   long long j = 0;
-  int hcnt = 0, hcur = 0;       // chunk position inside the current head
-  for (; j < J; ++j, advance(cc)) {
-    if (issued < J) {
+  int hcnt = 0, hcur = 0;  // chunk position inside the current head
+  for (;; ++j, advance(cc)) {
+    if (issuing) {
       // the stage of unit j - 1 has been consumed by every lane: refill it
       __syncwarp();
       fence_proxy_async_smem();
-      issue(pc);
-      advance(pc);
-      ++issued;
+      issue_next();
+    }
+    if (cc.u == 0) {
+      cc.t = tokq[cc.st];
+      if (cc.t >= N) break;
     }
     if (!mbar_wait_bounded(&wbars[cc.st], cc.ph)) {
       if (lane == 0) atomicOr(&g_warp_status, kStatusFullWaitTimeout);
@@ -416,11 +447,20 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
     }
   }
 
-  if (j < J) {
-    // gave up: let this warp's copies that are still in flight land first
-    for (long long i = j; i < issued; ++i, advance(cc))
-      if (!mbar_wait_bounded(&wbars[cc.st], cc.ph))
-        if (lane == 0) atomicOr(&g_warp_status, kStatusDrainTimeout);
+  // On a wait timeout, let this warp's copies still in flight land first
+  // (after a normal exit j == issued).
+  for (long long i = j; i < issued; ++i, advance(cc))
+    if (!mbar_wait_bounded(&wbars[cc.st], cc.ph))
+      if (lane == 0) atomicOr(&g_warp_status, kStatusDrainTimeout);
+
+  if (claim != nullptr && lane == 0) {
+    // the last warp to finish rewinds the counter pair for the next launch
+    __threadfence();
+    const unsigned long long warps = static_cast<unsigned long long>(gridDim.x) * NW;
+    if (atomicAdd(claim + 1, 1ull) == warps - 1) {
+      atomicExch(claim, 0ull);
+      atomicExch(claim + 1, 0ull);
+    }
   }
 
   if constexpr (BWD) {
@@ -518,7 +558,8 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
   const int max_warps = bwd ? 16 : 20;
   int nw = std::min(max_warps, std::max(1, env_int_w("ATTNRES_STREAM_WARPS", max_warps)));
   for (; nw >= 1; --nw) {
-    size_t off = kStreamMaxWarps * kStreamMaxStages * sizeof(uint64_t) + 6 * sizeof(void*) * base.S;
+    size_t off = kStreamMaxWarps * kStreamMaxStages * (sizeof(uint64_t) + sizeof(long long)) +
+                 6 * sizeof(void*) * base.S;
     off += sizeof(float) * static_cast<size_t>(nw) * (base.R + base.H + base.S);
     off = align_up(off, 128);
     const size_t wscr_off = off;
@@ -588,6 +629,39 @@ static void fill_stream_common(LridArgs& a, const LridPlan& p, const TmaLayout& 
   a.out_eps = io.out_eps;
 }
 
+// Counter pairs of the dynamic token schedule, one per launch in a rotation of
+// kClaimSlots (zero at module load; each launch leaves its pair at zero). A
+// pair is reused kClaimSlots launches later, so launches on concurrent
+// streams do not share a pair; a captured graph keeps the pair it was given,
+// and replays of one graph are ordered.
+constexpr int kClaimSlots = 64;
+constexpr int kClaimMaxDevices = 64;
+static __device__ unsigned long long g_claim[kClaimSlots * 2];
+
+static cudaError_t claim_slot(unsigned long long** slot) {
+  static std::atomic<unsigned long long*> base[kClaimMaxDevices];
+  static std::atomic<unsigned> seq{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kClaimMaxDevices) return cudaErrorInvalidDevice;
+  unsigned long long* b = base[dev].load();
+  if (b == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_claim);
+    if (e != cudaSuccess) return e;
+    b = static_cast<unsigned long long*>(p);
+    base[dev].store(b);
+  }
+  *slot = b + 2 * (seq.fetch_add(1) % kClaimSlots);
+  return cudaSuccess;
+}
+
+static bool dynamic_schedule() {
+  const char* v = getenv("ATTNRES_STREAM_SCHEDULE");
+  return !(v && strcmp(v, "static") == 0);
+}
+
 cudaError_t lrid_warp_forward_launch(int dtype, const LridPlan& p, const TmaLayout& L, int nw,
                                      const LridIO& io, cudaStream_t st) {
   LridArgs a{};
@@ -599,6 +673,7 @@ cudaError_t lrid_warp_forward_launch(int dtype, const LridPlan& p, const TmaLayo
   int grid = 0;
   cudaError_t e = stream_shape(dtype, p, L, false, &fn, &grid);
   if (e != cudaSuccess) return e;
+  if (dynamic_schedule() && (e = claim_slot(&a.claim)) != cudaSuccess) return e;
   fn<<<grid, nw * 32, L.smem_bytes, st>>>(a);
   return cudaGetLastError();
 }

@@ -316,3 +316,38 @@ def test_reference_library_op_with_aux_and_output_norm():
     assert_close("dq", to_np(q.grad).reshape(-1), grads["dq"], torch.float32, sum_terms=B * T)
     assert_close("dV0", to_np(values[0].grad).reshape(B * T, D), grads["dV"][0], torch.float32)
     assert_close("dK2", to_np(keys[2].grad).reshape(B * T, R), grads["dK"][2], torch.float32)
+
+
+def test_lrid_forward_token_schedule_static_equals_dynamic(kernel_path, monkeypatch):
+    """The streaming forward claims tokens from a global counter (dynamic
+    schedule); its rows must match the static round-robin schedule bit for bit,
+    across repeated launches (the counter rewinds itself) and graph replays."""
+    if kernel_path != "auto":
+        pytest.skip("schedule applies to the streaming kernel (auto path)")
+    ops = _ops()
+    S, B, T, D, R, H = 9, 3, 2731, 1024, 64, 1
+    torch.manual_seed(1)
+    values = [torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
+    keys = [torch.randn(B, T, R, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
+    q = torch.randn(H, R // H, device="cuda") * 0.02
+
+    def fwd():
+        return ops.lrid_attention_residual_read(values, keys, q, H, 0.125, True)
+
+    monkeypatch.setenv("ATTNRES_STREAM_SCHEDULE", "static")
+    ref = fwd()
+    monkeypatch.setenv("ATTNRES_STREAM_SCHEDULE", "dynamic")
+    for _ in range(3):
+        assert torch.equal(fwd(), ref)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        fwd()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        out = fwd()
+    for _ in range(3):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
