@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
   const int KL = L.key_lanes;
   const bool has_qd = a.qmode != ATTNRES_QUERY_STATIC;
   const int SH = S * H;
+  const int SP = (S + 3) & ~3;  // per-head row stride of the scratch arrays (16-byte rows)
+  const int HSP = H * SP;
   const int C = d / CW, cph = dv / CW, U1 = C + 1;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);  // [NW][NSW]
@@ -85,10 +87,10 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
   // per-warp scratch: logit | alpha | kinv | qk | dw (each [H][S] fp32), then
   // (backward) a copy of the token's key rows [S][R] and query [R]
   float* sm_logit = reinterpret_cast<float*>(wscr0 + static_cast<size_t>(w) * L.off_qd);
-  float* sm_alpha = sm_logit + SH;
-  float* sm_kinv = sm_alpha + SH;
-  float* sm_qk = sm_kinv + SH;
-  float* sm_dw = sm_qk + SH;
+  float* sm_alpha = sm_logit + HSP;
+  float* sm_kinv = sm_alpha + HSP;
+  float* sm_qk = sm_kinv + HSP;
+  float* sm_dw = sm_qk + HSP;
   T* kcopy = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(sm_logit) + L.off_v);
   T* qcopy = kcopy + S * R;
   unsigned char* ring = stage0 + static_cast<size_t>(w) * NSW * L.stage_bytes;
@@ -101,12 +103,16 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
   const long long N = P.N;
   const long long step = static_cast<long long>(NW) * gridDim.x;
   long long stat_next = blockIdx.x + static_cast<long long>(w) * gridDim.x;
+  // Lane 0 keeps one claim in flight, so the atomic's round trip overlaps a
+  // token's work instead of stalling the copy issue.
   unsigned long long* claim = a.claim;
+  unsigned long long claimed = 0;
+  if (claim != nullptr && lane == 0) claimed = atomicAdd(claim, 1ull);
   auto next_token = [&]() -> long long {
     if (claim != nullptr) {
-      unsigned long long v = 0;
-      if (lane == 0) v = atomicAdd(claim, 1ull);
-      return static_cast<long long>(__shfl_sync(0xffffffffu, v, 0));
+      const unsigned long long v = __shfl_sync(0xffffffffu, claimed, 0);
+      if (lane == 0) claimed = atomicAdd(claim, 1ull);
+      return static_cast<long long>(v);
     }
     const long long t = stat_next;
     stat_next += step;
@@ -133,7 +139,14 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
     }
   };
   // Issue the copies of the unit at cursor c: lane 0 posts the byte count,
-  // then lane i copies row i (the whole warp calls this, converged).
+  // then lane i copies the rows of sources i, i + 32, ... (the whole warp
+  // calls this, converged). Each lane forms its sources' value-row pointers
+  // once per token, when the token's key unit is issued.
+  constexpr int NL = (SMAX + 31) / 32;
+  const T* vrow[NL];
+#pragma unroll
+  for (int i = 0; i < NL; ++i) vrow[i] = nullptr;
+  const T* grow = nullptr;  // this token's grad-output row (backward)
   auto issue = [&](const Cursor& c) {
     const long long t = c.t;
     unsigned char* st = ring + static_cast<size_t>(c.st) * L.stage_bytes;
@@ -142,15 +155,27 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
       const uint32_t kb = R * sizeof(T);
       if (lane == 0) mbar_arrive_expect_tx(bar, S * kb + (has_qd ? kb : 0));
       __syncwarp();
-      for (int s = lane; s < S; s += 32) bulk_g2s(st + s * kb, sk[s] + t * sks[s], kb, bar);
+#pragma unroll
+      for (int i = 0; i < NL; ++i) {
+        const int s = lane + 32 * i;
+        if (s < S) {
+          bulk_g2s(st + s * kb, sk[s] + t * sks[s], kb, bar);
+          vrow[i] = sv[s] + t * svs[s];
+        }
+      }
       if (has_qd && lane == (S & 31)) bulk_g2s(st + S * kb, qsrc + t * R, kb, bar);
+      if (BWD) grow = gsrc + t * d;
     } else {
       const int c0 = (c.u - 1) * CW;
       const uint32_t cb = CW * sizeof(T);
       if (lane == 0) mbar_arrive_expect_tx(bar, S * cb + (BWD ? cb : 0));
       __syncwarp();
-      for (int s = lane; s < S; s += 32) bulk_g2s(st + s * cb, sv[s] + t * svs[s] + c0, cb, bar);
-      if (BWD && lane == (S & 31)) bulk_g2s(st + S * cb, gsrc + t * d + c0, cb, bar);
+#pragma unroll
+      for (int i = 0; i < NL; ++i) {
+        const int s = lane + 32 * i;
+        if (s < S) bulk_g2s(st + s * cb, vrow[i] + c0, cb, bar);
+      }
+      if (BWD && lane == (S & 31)) bulk_g2s(st + S * cb, grow + c0, cb, bar);
     }
   };
 
@@ -264,30 +289,30 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
         if (seg < SH && kl == 0) {
           const float kinv = a.key_norm ? rsqrtf(ss / dk + a.key_eps) : 1.f;
           const float qk = dot * kinv;
-          sm_logit[kh * S + s] = qk * a.scale + (a.bias ? a.bias[s] : 0.f);
-          sm_kinv[kh * S + s] = kinv;
-          sm_qk[kh * S + s] = qk;
+          sm_logit[kh * SP + s] = qk * a.scale + (a.bias ? a.bias[s] : 0.f);
+          sm_kinv[kh * SP + s] = kinv;
+          sm_qk[kh * SP + s] = qk;
         }
       }
       __syncwarp();
       for (int h = 0; h < H; ++h) {
-        const float* lg = sm_logit + h * S;
+        const float* lg = sm_logit + h * SP;
         const float l0 = lane < S ? lg[lane] : -INFINITY;
         const float l1 = lane + 32 < S ? lg[lane + 32] : -INFINITY;
         const float m = warp_max(fmaxf(l0, l1));
         const float e0 = lane < S ? expf(l0 - m) : 0.f;
         const float e1 = lane + 32 < S ? expf(l1 - m) : 0.f;
         const float sum = warp_sum(e0 + e1);
-        if (lane < S) sm_alpha[h * S + lane] = e0 / sum;
-        if (lane + 32 < S) sm_alpha[h * S + lane + 32] = e1 / sum;
+        if (lane < S) sm_alpha[h * SP + lane] = e0 / sum;
+        if (lane + 32 < S) sm_alpha[h * SP + lane + 32] = e1 / sum;
         if (!BWD) {
           if (a.alpha_out) {
             if (lane < S) a.alpha_out[(t * H + h) * S + lane] = e0 / sum;
             if (lane + 32 < S) a.alpha_out[(t * H + h) * S + lane + 32] = e1 / sum;
           }
           if (a.kinv_out) {
-            if (lane < S) a.kinv_out[(t * H + h) * S + lane] = sm_kinv[h * S + lane];
-            if (lane + 32 < S) a.kinv_out[(t * H + h) * S + lane + 32] = sm_kinv[h * S + lane + 32];
+            if (lane < S) a.kinv_out[(t * H + h) * S + lane] = sm_kinv[h * SP + lane];
+            if (lane + 32 < S) a.kinv_out[(t * H + h) * S + lane + 32] = sm_kinv[h * SP + lane + 32];
           }
         }
       }
@@ -301,22 +326,34 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
     const int h = hcur;
     const int col = c * CW + lane * VEC;
     const T* vt = reinterpret_cast<const T*>(st) + lane * VEC;  // + s * CW
-    const float* al = sm_alpha + h * S;
+    const float* al = sm_alpha + h * SP;
     if constexpr (!BWD) {
       float acc[VEC];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+      // sources in blocks of four: one 16-byte read of their weights, four
+      // value packs, then the packed FMAs; the last block is guarded
+      int s0 = 0;
+      for (; s0 + 4 <= S; s0 += 4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(al + s0);
+        Pack<T, VEC> r4[4];
 #pragma unroll
-      for (int s0 = 0; s0 < SMAX; s0 += 4) {
-        if (s0 < S) {
-          Pack<T, VEC> r4[4];
+        for (int jj = 0; jj < 4; ++jj) r4[jj] = lds_pack<T, VEC>(vt + (s0 + jj) * CW);
+        axpy_pack<T, VEC>(acc, w4.x, r4[0]);
+        axpy_pack<T, VEC>(acc, w4.y, r4[1]);
+        axpy_pack<T, VEC>(acc, w4.z, r4[2]);
+        axpy_pack<T, VEC>(acc, w4.w, r4[3]);
+      }
+      if (s0 < S) {
+        const float4 w4 = *reinterpret_cast<const float4*>(al + s0);
+        const float wj[4] = {w4.x, w4.y, w4.z, w4.w};
+        Pack<T, VEC> r4[4];
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj)
-            if (s0 + jj < S) r4[jj] = lds_pack<T, VEC>(vt + (s0 + jj) * CW);
+        for (int jj = 0; jj < 4; ++jj)
+          if (s0 + jj < S) r4[jj] = lds_pack<T, VEC>(vt + (s0 + jj) * CW);
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj)
-            if (s0 + jj < S) axpy_pack<T, VEC>(acc, al[s0 + jj], r4[jj]);
-        }
+        for (int jj = 0; jj < 4; ++jj)
+          if (s0 + jj < S) axpy_pack<T, VEC>(acc, wj[jj], r4[jj]);
       }
       store_pack<T, VEC>(static_cast<T*>(a.out) + t * d + col, acc);
       if (++hcnt == cph) {
@@ -359,7 +396,7 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
         for (int s = 0; s < SMAX; ++s) {
           if (s < S) {
             const float dw = warp_sum(dwp[s]);
-            if (lane == 0) sm_dw[h * S + s] = dw;
+            if (lane == 0) sm_dw[h * SP + s] = dw;
           }
           dwp[s] = 0.f;
         }
@@ -369,14 +406,14 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
         __syncwarp();
         // ---- dlogit per head (stored over the logits) -------------------------
         for (int hh = 0; hh < H; ++hh) {
-          const float* alp = sm_alpha + hh * S;
-          const float* dwh = sm_dw + hh * S;
+          const float* alp = sm_alpha + hh * SP;
+          const float* dwh = sm_dw + hh * SP;
           const float a0 = lane < S ? alp[lane] : 0.f, a1 = lane + 32 < S ? alp[lane + 32] : 0.f;
           const float w0 = lane < S ? dwh[lane] : 0.f, w1 = lane + 32 < S ? dwh[lane + 32] : 0.f;
           const float wd = warp_sum(a0 * w0 + a1 * w1);
           const float dl0 = a0 * (w0 - wd), dl1 = a1 * (w1 - wd);
-          if (lane < S) sm_logit[hh * S + lane] = dl0;
-          if (lane + 32 < S) sm_logit[hh * S + lane + 32] = dl1;
+          if (lane < S) sm_logit[hh * SP + lane] = dl0;
+          if (lane + 32 < S) sm_logit[hh * SP + lane + 32] = dl1;
           dbias0 += dl0;
           dbias1 += dl1;
         }
@@ -389,9 +426,9 @@ __global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const _
           const int seg = r * G + gidx;
           const int s = seg >> hshift;
           if (seg < SH) {
-            const float c1 = sm_logit[kh * S + s] * a.scale;
-            const float kinv = sm_kinv[kh * S + s];
-            const float c2 = a.key_norm ? c1 * sm_qk[kh * S + s] / dk : 0.f;
+            const float c1 = sm_logit[kh * SP + s] * a.scale;
+            const float kinv = sm_kinv[kh * SP + s];
+            const float c2 = a.key_norm ? c1 * sm_qk[kh * SP + s] / dk : 0.f;
 #pragma unroll
             for (int pk = 0; pk < KP; ++pk) {
               const Pack<T, VEC> kr = lds_pack<T, VEC>(kcopy + s * R + kcol + pk * VEC);
@@ -548,11 +585,10 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
   int dev = 0, cap = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   if (cudaDeviceGetAttribute(&cap, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return false;
-  const size_t SH = static_cast<size_t>(base.S) * base.H;
   const size_t key_unit = static_cast<size_t>(base.S) * base.R * esz + (has_qd ? base.R * esz : 0);
   const size_t chunk_unit = static_cast<size_t>(base.S) * CW * esz + (bwd ? CW * esz : 0);
   const size_t sb = align_up(std::max(key_unit, chunk_unit), 128);
-  const size_t kcopy_off = align_up(5 * SH * sizeof(float), 16);
+  const size_t kcopy_off = align_up(5 * static_cast<size_t>(base.H) * ((base.S + 3) & ~3) * sizeof(float), 16);
   const size_t wscr = align_up(kcopy_off + (bwd ? key_unit : 0), 128);
   const int nsw = std::max(2, std::min(kStreamMaxStages, env_int_w("ATTNRES_STREAM_STAGES", 2)));
   const int max_warps = bwd ? 16 : 20;
