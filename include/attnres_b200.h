@@ -216,6 +216,31 @@ int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, in
                                          int value_norm, void* stream);
 
 /*
+ * Fused backward of the key projection on the tensor cores, for the one-pass
+ * key-from-value read backward (the read ran with grad_values == NULL):
+ *   dKs = inv * dK,  coef = inv * <dKs, key> / d
+ *   grad_values[s][n] = alpha[n,h,s] * grad_output[n] + (dKs_s @ W)[n] - V_s[n] * coef[s][n]
+ *   grad_weight (float [R][d], overwritten) = sum_s dKs_s^T @ V_s
+ * grad_keys: one dtype [N, R] dense array per source; keys dtype [S][N][R];
+ * weight: dtype [R, d] with row stride weight_row_stride. f16/bf16, R == 64,
+ * (value_dim / num_heads) % 128 == 0, num_sources <= 24. The workspace query
+ * returns 0 when the shapes do not fit (use attnres_lrid_key_projection_backward
+ * with a separate dn = dK @ W then). Deterministic. Replaces the autograd
+ * backward of model.py:344-356 (rms_norm + value_key_proj), weight gradient
+ * included.
+ */
+size_t attnres_lrid_key_projection_backward_tc_workspace_bytes(int num_sources, int64_t num_tokens, int value_dim,
+                                                               int key_dim, int num_heads, int dtype);
+int attnres_lrid_key_projection_backward_tc(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                            int num_heads, int dtype, const void* const* values,
+                                            const int64_t* value_row_strides, const void* weight,
+                                            int64_t weight_row_stride, const void* const* grad_keys,
+                                            const void* keys, const float* inv_rms, const void* grad_output,
+                                            const float* alpha, int value_norm, void* const* grad_values,
+                                            float* grad_weight, void* workspace, size_t workspace_bytes,
+                                            void* stream);
+
+/*
  * Cached-logit block read ("phase 1"): Q reads of the same S sources whose
  * logits were computed once. Replaces attention_residual_phase1_from_logits
  * (attnres_ops.py:3910-3961) and its Triton kernels (:933-989, :1069-1140).

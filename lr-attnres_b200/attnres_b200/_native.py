@@ -35,6 +35,8 @@ EXPORTED_SYMBOLS = (
     "attnres_lrid_backward_noalloc",
     "attnres_lrid_key_projection",
     "attnres_lrid_key_projection_backward",
+    "attnres_lrid_key_projection_backward_tc_workspace_bytes",
+    "attnres_lrid_key_projection_backward_tc",
     "attnres_phase1_forward",
     "attnres_phase1_backward",
     "attnres_noalloc_scratch_bytes",
@@ -101,6 +103,16 @@ def load(path=None):
     L.attnres_lrid_key_projection.argtypes = [I, I64, I, I, I, PP, PI64, P, I64, I, F, P, P, P]
     L.attnres_lrid_key_projection_backward.restype = I
     L.attnres_lrid_key_projection_backward.argtypes = [I, I64, I, I, I, I, PP, PI64, PP, P, P, P, P, P, P, I, P]
+    L.attnres_lrid_key_projection_backward_tc_workspace_bytes.restype = SZ
+    L.attnres_lrid_key_projection_backward_tc_workspace_bytes.argtypes = [I, I64, I, I, I, I]
+    L.attnres_lrid_key_projection_backward_tc.restype = I
+    L.attnres_lrid_key_projection_backward_tc.argtypes = [
+        I, I64, I, I, I, I,          # S, N, d, R, H, dtype
+        PP, PI64, P, I64,            # values, strides, weight, weight row stride
+        PP, P, P, P, P, I,           # grad_keys, keys, inv_rms, grad_output, alpha, value_norm
+        PP, P, P, SZ,                # grad_values, grad_weight, workspace, workspace bytes
+        P,                           # stream
+    ]
     L.attnres_phase1_forward.restype = I
     L.attnres_phase1_forward.argtypes = [I, I, I64, I, I, PP, PI64, P, I, I, F, P, P, P, P]
     L.attnres_phase1_backward.restype = I

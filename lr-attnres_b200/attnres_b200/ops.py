@@ -19,6 +19,7 @@ current stream through the C ABI. There is no CPU fallback: a CPU tensor is a
 RuntimeError.
 """
 import ctypes
+import os
 from typing import List, Optional, Sequence
 
 import torch
@@ -798,11 +799,33 @@ def lrid_kv_read_backward(
         output_inv_rms, num_heads, logit_scale, key_norm, int(output_norm), write_dv=not one_pass)
     n = _ntok(values[0])
     g_rows = grad_output.to(dtype).reshape(n, d).contiguous() if one_pass else None
+    device = values[0].device
+    if one_pass and os.environ.get("ATTNRES_KV_BWD", "tc") != "gemm":
+        # fused tensor-core projection backward: dV written once, dW in the same pass
+        with torch.cuda.device(device):
+            L = N.load()
+            ws_bytes = L.attnres_lrid_key_projection_backward_tc_workspace_bytes(
+                S, n, d, R, int(num_heads), _dtype_code(dtype))
+            if ws_bytes > 0:
+                rows, strides = _sources(values, d, dtype)
+                w = key_weight.to(dtype)
+                ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8)
+                dw = torch.empty((R, d), device=device, dtype=torch.float32)
+                gks = [g.reshape(n, R).contiguous() for g in gk]
+                rc = L.attnres_lrid_key_projection_backward_tc(
+                    S, n, d, R, int(num_heads), _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]),
+                    N.i64_array(strides), _ptr(w), w.stride(0), N.ptr_array([g.data_ptr() for g in gks]),
+                    _ptr(keys.reshape(S, n, R)), _ptr(value_inv_rms), _ptr(g_rows), _ptr(alpha.contiguous()),
+                    int(bool(value_norm)), N.ptr_array([g.data_ptr() for g in gv]), _ptr(dw), _ptr(ws), ws_bytes,
+                    _stream_ptr(device))
+                N.check(rc, "attnres_lrid_key_projection_backward_tc")
+                e = values[0].new_empty((0,), dtype=torch.float32)
+                return (gv, dw, dq, dgate if dgate is not None else e, dqd if dqd is not None else e.clone(),
+                        dbias if dbias is not None else e.clone())
     dk = torch.stack([g.reshape(n, R) for g in gk])  # [S, n, R]
     w = key_weight.to(dtype)
     dn = torch.matmul(dk, w)  # [S, n, d]: plain GEMM (cuBLAS)
     rows, strides = _sources(values, d, dtype)
-    device = values[0].device
     with torch.cuda.device(device):
         rc = N.load().attnres_lrid_key_projection_backward(
             S, n, d, R, int(num_heads), _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]),

@@ -148,6 +148,9 @@ int attnres_device_status(unsigned* status, int reset) {
   unsigned s3 = 0;
   if (e == cudaSuccess) e = attnres::read_warp_status(&s2, reset != 0);
   if (e == cudaSuccess) e = attnres::read_keyproj_status(&s3, reset != 0);
+  unsigned s4 = 0;
+  if (e == cudaSuccess) e = attnres::read_keyproj_bwd_status(&s4, reset != 0);
+  s3 |= s4;
   if (e != cudaSuccess) return cuda_fail(e, "attnres_device_status");
   *status = s1 | s2 | s3;
   return ATTNRES_OK;
@@ -466,6 +469,52 @@ int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, in
                                                       grad_normed, grad_keys, keys, inv_rms, grad_output,
                                                       alpha, value_norm, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_projection_backward launch");
+  return ATTNRES_OK;
+}
+
+size_t attnres_lrid_key_projection_backward_tc_workspace_bytes(int num_sources, int64_t num_tokens, int value_dim,
+                                                               int key_dim, int num_heads, int dtype) {
+  return attnres::keyproj_bwd_tc_workspace(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype);
+}
+
+int attnres_lrid_key_projection_backward_tc(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                            int num_heads, int dtype, const void* const* values,
+                                            const int64_t* value_row_strides, const void* weight,
+                                            int64_t weight_row_stride, const void* const* grad_keys,
+                                            const void* keys, const float* inv_rms, const void* grad_output,
+                                            const float* alpha, int value_norm, void* const* grad_values,
+                                            float* grad_weight, void* workspace, size_t workspace_bytes,
+                                            void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values,
+                         value_row_strides, nullptr, nullptr, false);
+  if (rc) return rc;
+  if (num_tokens == 0) return ATTNRES_OK;
+  const size_t need = attnres::keyproj_bwd_tc_workspace(num_sources, num_tokens, value_dim, key_dim, num_heads,
+                                                         dtype);
+  if (need == 0)
+    return fail(ATTNRES_ERR_UNSUPPORTED,
+                "fused projection backward needs f16/bf16, key_dim 64, value_dim/num_heads a multiple of 128, "
+                "at most 24 sources");
+  if (!weight || !grad_keys || !keys || !grad_output || !alpha || !grad_values || !grad_weight || !workspace ||
+      (value_norm && !inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "fused projection backward: NULL buffer");
+  if (workspace_bytes < need)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  if (weight_row_stride < value_dim) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "weight_row_stride < value_dim");
+  if (!aligned16(grad_output) || !aligned16(keys) || !aligned16(workspace))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_output, keys and workspace must be 16-byte aligned");
+  for (int s = 0; s < num_sources; ++s) {
+    if (!grad_keys[s] || !grad_values[s] || !aligned16(grad_keys[s]) || !aligned16(grad_values[s]))
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_keys[%d] / grad_values[%d] NULL or not 16-byte aligned", s,
+                  s);
+    if (!aligned16(values[s]) || (value_row_strides[s] * 2) % 16)
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "values[%d] must be 16-byte aligned with 16-byte row strides", s);
+  }
+  cudaError_t e = attnres::keyproj_bwd_tc_launch(
+      num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values, value_row_strides, weight,
+      weight_row_stride, grad_keys, keys, inv_rms, grad_output, alpha, value_norm, grad_values, grad_weight,
+      workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_projection_backward_tc launch");
   return ATTNRES_OK;
 }
 

@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "plan.h"
 #include "tma.cuh"
+#include "umma.cuh"
 
 namespace attnres {
 
@@ -44,55 +45,6 @@ struct KeyProjArgs {
   float eps;
   uint32_t idesc;
 };
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// K-major, 128-byte-swizzled operand tile: 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile) {
-  const uint32_t addr = smem_u32(tile);
-  uint64_t desc = 0;
-  desc |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);        // start address
-  desc |= static_cast<uint64_t>(1) << 16;                     // leading byte offset (unused, swizzled K-major)
-  desc |= static_cast<uint64_t>(1024 >> 4) << 32;             // stride byte offset
-  desc |= static_cast<uint64_t>(1) << 46;                     // descriptor version (sm_100)
-  desc |= static_cast<uint64_t>(2) << 61;                     // SWIZZLE_128B
-  return desc;
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      :
-      : "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 template <typename T>
 __global__ void __launch_bounds__(192, 1) keyproj_tc_kernel(const __grid_constant__ KeyProjArgs a) {
@@ -130,10 +82,7 @@ __global__ void __launch_bounds__(192, 1) keyproj_tc_kernel(const __grid_constan
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(tmem_cols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tmem_alloc(tmem_slot, tmem_cols);
   }
   tc_fence_before();
   __syncthreads();
@@ -272,8 +221,7 @@ __global__ void __launch_bounds__(192, 1) keyproj_tc_kernel(const __grid_constan
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
-                 : "memory");
+    tmem_dealloc(tmem_base, tmem_cols);
   }
 }
 
@@ -379,39 +327,6 @@ __global__ void __launch_bounds__(256) keyproj_bwd_combine_kernel(const __grid_c
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-static bool encode_2d(CUtensorMap* map, int dtype, const void* ptr, long long rows, int cols, long long row_stride,
-                      int box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  const int esz = 2;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * esz};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kKpK), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapDataType dt =
-      dtype == ATTNRES_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 static bool tc_eligible(int S, long long N, int d, int R, int dtype, const void* const* values, const int64_t* vstr,
                         const void* w, long long w_stride) {
   if (dtype == ATTNRES_DTYPE_F32 || S > kKpMaxSources || N < 1) return false;

@@ -157,6 +157,16 @@ cudaError_t keyproj_bwd_combine_launch(int S, long long N, int d, int R, int H, 
                                        const void* keys, const float* inv_rms, const void* g,
                                        const float* alpha, int value_norm, cudaStream_t st);
 cudaError_t read_keyproj_status(unsigned* status, bool reset);
+
+// Fused tcgen05 backward of the key projection (keyproj_bwd.cu). Workspace 0
+// means the shapes do not fit the kernel.
+size_t keyproj_bwd_tc_workspace(int S, long long N, int d, int R, int H, int dtype);
+cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int dtype, const void* const* values,
+                                  const int64_t* vstr, const void* w, long long w_stride,
+                                  const void* const* grad_keys, const void* keys, const float* inv_rms,
+                                  const void* g, const float* alpha, int value_norm, void* const* grad_values,
+                                  float* grad_weight, void* workspace, size_t workspace_bytes, cudaStream_t st);
+cudaError_t read_keyproj_bwd_status(unsigned* status, bool reset);
 }  // namespace attnres
 
 namespace attnres {
