@@ -13,18 +13,21 @@
 //   * kpb_transpose_w_kernel: Wt = W^T (dtype [d][64]);
 //   * keyproj_bwd_tc_kernel, persistent, one 128-column slice of d per CTA.
 //     The CTA walks its token tiles (128 tokens) and, inside each, the S
-//     sources, so the slice of g is re-read from L2 and the slice of W (Wt,
-//     16 KB) stays in shared memory:
+//     sources; the slice of g is loaded once per token tile and the slice of W
+//     (Wt, 16 KB) once per CTA:
 //       - warp 0 (one thread): TMA loads (128-byte swizzle, no multicast) of
-//         the dKs tile [128 x 64], the V_s slice [128 x 128] and the g slice
-//         [128 x 128] into a two-stage ring;
+//         the dKs tile [128 x 64] and the V_s slice [128 x 128] into a
+//         three-stage ring, and of the g slice into a double buffer;
 //       - warp 1 (one thread): tcgen05.mma kind::f16 M=128:
 //           dn[128 tok x 128 col]  = dKs (K-major) x Wt (K-major), N=128, into
 //             one of two TMEM accumulators;
 //           dWt[128 col x 64]     += V^T (MN-major) x dKs (MN-major), N=64, a
 //             TMEM accumulator that lives across all of the CTA's tiles;
-//       - warps 2-5 (one token row per thread): dV = alpha g + dn - V coef
-//         from TMEM and the staged V / g tiles, 16-byte stores.
+//       - warps 3-10 (one token row x 64 columns per thread, two warps per
+//         TMEM lane quarter): dV = alpha g + dn - V coef from TMEM and the
+//         staged tiles, written over the V tile once the dWt MMA has read it;
+//       - warp 2: TMA store of each finished dV tile, one tile behind the
+//         epilogue, then frees the stage.
 //     At the end each CTA writes its dWt slice to a partial buffer;
 //   * kpb_reduce_dw_kernel sums the partials of each slice in a fixed order
 //     (deterministic) into dW (f32 [64][d]).
@@ -45,46 +48,54 @@ constexpr int kKpbMaxSources = 24;
 constexpr int kKpbRows = 128;   // tokens per tile (UMMA M of dn)
 constexpr int kKpbCols = 128;   // columns of d per CTA slice (UMMA N of dn, M of dWt)
 constexpr int kKpbR = 64;       // key rank
-constexpr int kKpbStages = 2;
-constexpr uint32_t kKpbKBytes = kKpbRows * kKpbR * 2;        // dKs tile, 16 KB
-constexpr uint32_t kKpbAtom = kKpbRows * kTmaBoxCols * 2;     // one 64-column box, 16 KB
-constexpr uint32_t kKpbStageBytes = kKpbKBytes + 4 * kKpbAtom;  // dKs | V (2 boxes) | g (2 boxes)
-constexpr uint32_t kKpbTmemCols = 512;                        // dn x2 (256) + dWt (64), power of two
+constexpr int kKpbStages = 3;
+constexpr uint32_t kKpbKBytes = kKpbRows * kKpbR * 2;          // dKs tile, 16 KB
+constexpr uint32_t kKpbAtom = kKpbRows * kTmaBoxCols * 2;       // one 64-column box, 16 KB
+constexpr uint32_t kKpbStageBytes = kKpbKBytes + 2 * kKpbAtom;  // dKs | V (2 boxes; dV after the epilogue)
+constexpr uint32_t kKpbGBytes = 2 * kKpbAtom;                   // g slice of a token tile
+constexpr uint32_t kKpbTmemCols = 512;                          // dn x2 (256) + dWt (64), power of two
+constexpr int kKpbEpiWarps = 8;                                // two per TMEM lane quarter
+constexpr int kKpbThreads = (3 + kKpbEpiWarps) * 32;            // producer, MMA, store, epilogue
+constexpr size_t kKpbSmem = 1024 + kKpbKBytes + 2 * kKpbGBytes + kKpbStages * kKpbStageBytes + 256;
 
 static __device__ unsigned int g_kpb_status = 0;
 
 struct KpbArgs {
-  CUtensorMap vmap[kKpbMaxSources];  // V_s as [N rows, d cols]
-  CUtensorMap gmap;                  // g as [N, d]
-  CUtensorMap kmap;                  // dKs as [S][N][64]
-  CUtensorMap wtmap;                 // Wt as [d, 64]
-  void* gv[kKpbMaxSources];          // dV_s [N, d] dense
-  const float* alpha;                // [N][H][S]
-  const float* coef;                 // [S][N]
-  float* partials;                   // [grid][128][64]
+  CUtensorMap vmap[kKpbMaxSources];   // V_s as [N rows, d cols]
+  CUtensorMap gvmap[kKpbMaxSources];  // dV_s as [N, d] (TMA stores)
+  CUtensorMap gmap;                   // g as [N, d]
+  CUtensorMap kmap;                   // dKs as [S][N][64]
+  CUtensorMap wtmap;                  // Wt as [d, 64]
+  const float* alpha;                 // [N][H][S]
+  const float* coef;                  // [S][N]
+  float* partials;                    // [grid][128][64]
   long long N;
   int S, d, H, nch, ntt;
   uint32_t idesc_dn, idesc_dw;
 };
 
 template <typename T>
-__global__ void __launch_bounds__(192, 1) keyproj_bwd_tc_kernel(const __grid_constant__ KpbArgs a) {
+__global__ void __launch_bounds__(kKpbThreads, 1) keyproj_bwd_tc_kernel(const __grid_constant__ KpbArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* wt_tile = base;                  // [128 cols][64] K-major, 16 KB
-  unsigned char* stages = base + kKpbKBytes;      // kKpbStages x kKpbStageBytes
+  unsigned char* gbuf = base + kKpbKBytes;        // 2 x g slice
+  unsigned char* stages = gbuf + 2 * kKpbGBytes;  // kKpbStages x (dKs | V)
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + kKpbStages * kKpbStageBytes);
-  uint64_t* empty = full + kKpbStages;
-  uint64_t* acc_full = empty + kKpbStages;
+  uint64_t* empty = full + kKpbStages;   // stage free: its dV tile has been read by the store
+  uint64_t* vfree = empty + kKpbStages;  // the dWt MMA has finished reading the stage's V
+  uint64_t* acc_full = vfree + kKpbStages;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* wt_full = acc_empty + 2;
+  uint64_t* gfull = acc_empty + 2;
+  uint64_t* gempty = gfull + 2;
+  uint64_t* wt_full = gempty + 2;
   uint64_t* done = wt_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ch = blockIdx.x % a.nch;       // column slice of this CTA
-  const int grp = blockIdx.x / a.nch;      // token tiles grp, grp + G, ...
+  const int ch = blockIdx.x % a.nch;   // column slice of this CTA
+  const int grp = blockIdx.x / a.nch;  // token tiles grp, grp + G, ...
   const int G = gridDim.x / a.nch;
   const int S = a.S;
   const int c_base = ch * kKpbCols;
@@ -92,11 +103,14 @@ __global__ void __launch_bounds__(192, 1) keyproj_bwd_tc_kernel(const __grid_con
   if (threadIdx.x == 0) {
     for (int i = 0; i < kKpbStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1 + 4);  // MMA commit + 4 epilogue warps
+      mbar_init(&empty[i], 1);
+      mbar_init(&vfree[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], kKpbEpiWarps);
+      mbar_init(&gfull[i], 1);
+      mbar_init(&gempty[i], kKpbEpiWarps);
     }
     mbar_init(wt_full, 1);
     mbar_init(done, 1);
@@ -116,8 +130,20 @@ __global__ void __launch_bounds__(192, 1) keyproj_bwd_tc_kernel(const __grid_con
       mbar_arrive_expect_tx(wt_full, kKpbKBytes);
       tma_load_2d(wt_tile, &a.wtmap, 0, c_base, wt_full);
       long long it = 0;
+      int k = 0;  // token tiles of this CTA so far
       bool ok = true;
-      for (int tt = grp; tt < a.ntt && ok; tt += G) {
+      for (int tt = grp; tt < a.ntt && ok; tt += G, ++k) {
+        const int t0 = tt * kKpbRows;
+        const int gb = k & 1;
+        if (*abort_flag || !mbar_wait_bounded(&gempty[gb], static_cast<uint32_t>(((k >> 1) & 1) ^ 1))) {
+          atomicOr(&g_kpb_status, kStatusEmptyWaitTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        unsigned char* gp = gbuf + gb * kKpbGBytes;
+        mbar_arrive_expect_tx(&gfull[gb], kKpbGBytes);
+        tma_load_2d(gp, &a.gmap, c_base, t0, &gfull[gb]);
+        tma_load_2d(gp + kKpbAtom, &a.gmap, c_base + kTmaBoxCols, t0, &gfull[gb]);
         for (int s = 0; s < S; ++s, ++it) {
           const int st = static_cast<int>(it % kKpbStages);
           const uint32_t par = static_cast<uint32_t>((it / kKpbStages) & 1);
@@ -128,19 +154,19 @@ __global__ void __launch_bounds__(192, 1) keyproj_bwd_tc_kernel(const __grid_con
             break;
           }
           unsigned char* sp = stages + st * kKpbStageBytes;
-          const int t0 = tt * kKpbRows;
           mbar_arrive_expect_tx(&full[st], kKpbStageBytes);
           tma_load_3d(sp, &a.kmap, 0, t0, s, &full[st]);
           tma_load_2d(sp + kKpbKBytes, &a.vmap[s], c_base, t0, &full[st]);
           tma_load_2d(sp + kKpbKBytes + kKpbAtom, &a.vmap[s], c_base + kTmaBoxCols, t0, &full[st]);
-          tma_load_2d(sp + kKpbKBytes + 2 * kKpbAtom, &a.gmap, c_base, t0, &full[st]);
-          tma_load_2d(sp + kKpbKBytes + 3 * kKpbAtom, &a.gmap, c_base + kTmaBoxCols, t0, &full[st]);
         }
       }
-      if (!ok) {
+      if (*abort_flag) {
         // let the copies already issued land before the CTA can exit
         for (long long j = (it > kKpbStages ? it - kKpbStages : 0); j < it; ++j)
           if (!mbar_wait_bounded(&full[j % kKpbStages], static_cast<uint32_t>((j / kKpbStages) & 1)))
+            atomicOr(&g_kpb_status, kStatusDrainTimeout);
+        for (int j = (k > 2 ? k - 2 : 0); j < k; ++j)
+          if (!mbar_wait_bounded(&gfull[j & 1], static_cast<uint32_t>((j >> 1) & 1)))
             atomicOr(&g_kpb_status, kStatusDrainTimeout);
       }
       if (!mbar_wait_bounded(wt_full, 0)) atomicOr(&g_kpb_status, kStatusDrainTimeout);
@@ -183,7 +209,7 @@ __global__ void __launch_bounds__(192, 1) keyproj_bwd_tc_kernel(const __grid_con
 #pragma unroll
             for (int k = 0; k < kKpbRows / 16; ++k)
               umma_f16(d_dw, dv + 128 * k, dkm + 128 * k, a.idesc_dw, (it > 0 || k > 0) ? 1u : 0u);
-            umma_commit(&empty[st]);
+            umma_commit(&vfree[st]);
             issued_any = true;
           }
         }
@@ -191,74 +217,120 @@ __global__ void __launch_bounds__(192, 1) keyproj_bwd_tc_kernel(const __grid_con
       umma_commit(done);
       if (issued_any && !mbar_wait_bounded(done, 0)) atomicOr(&g_kpb_status, kStatusDrainTimeout);
     }
+  } else if (warp == 2) {
+    // ---------------- dV tile stores (one tile behind the epilogue) -------------
+    // Meets the epilogue warps at named barrier 2 once per tile (the OR of
+    // their stop predicates makes every participant leave on the same tile),
+    // then stores the tile, waits until the TMA has read it and frees the stage.
+    long long it = 0;
+    bool stopped = !has_tiles;
+    for (int tt = grp; tt < a.ntt && !stopped; tt += G) {
+      const int t0 = tt * kKpbRows;
+      for (int s = 0; s < S; ++s, ++it) {
+        stopped = consumer_sync_or(kKpbEpiWarps * 32 + 32, *abort_flag != 0);
+        if (stopped) break;
+        if (lane == 0) {
+          const int st = static_cast<int>(it % kKpbStages);
+          const unsigned char* tile = stages + st * kKpbStageBytes + kKpbKBytes;
+          tma_store_2d(&a.gvmap[s], c_base, t0, tile);
+          tma_store_2d(&a.gvmap[s], c_base + kTmaBoxCols, t0, tile + kKpbAtom);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+          mbar_arrive(&empty[st]);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) bulk_wait_group0();
   } else {
-    // ---------------- epilogue: 4 warps, one token row per thread ---------------
-    const int q = warp & 3;         // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;  // token row of the tile / column row of dWt
+    // ---------------- epilogue: 8 warps, one token row x 64 columns per thread ---
+    // dV overwrites the V half-row it was computed from (the dWt MMA has read it
+    // by then: vfree), so the stage's V boxes become the dV tile of the store.
+    // A failed (timed-out) wait never skips named barrier 2: every epilogue warp
+    // reaches it each tile.
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = (warp - 3) >> 2;     // 64-column half (= V box) of the slice
+    const int row = q * 32 + lane;        // token row of the tile / column row of dWt
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int dvh = a.d / a.H;
     const int h = c_base / dvh;
     long long it = 0;
-    bool ok = has_tiles;
-    for (int tt = grp; tt < a.ntt && ok; tt += G) {
-      const long long t = static_cast<long long>(tt) * kKpbRows + row;
+    int k = 0;
+    bool stopped = !has_tiles;
+    for (int tt = grp; tt < a.ntt && !stopped; tt += G, ++k) {
+      const int t0 = tt * kKpbRows;
+      const long long t = static_cast<long long>(t0) + row;
       const bool live = t < a.N;
+      const int gb = k & 1;
+      bool good = !*abort_flag && mbar_wait_bounded(&gfull[gb], static_cast<uint32_t>((k >> 1) & 1));
+      if (!good) *abort_flag = 1;
+      const unsigned char* grow = gbuf + gb * kKpbGBytes + half * kKpbAtom + row * 128;
       for (int s = 0; s < S; ++s, ++it) {
         const int st = static_cast<int>(it % kKpbStages);
         const int ab = static_cast<int>(it & 1);
-        if (*abort_flag || !mbar_wait_bounded(&full[st], static_cast<uint32_t>((it / kKpbStages) & 1)) ||
-            !mbar_wait_bounded(&acc_full[ab], static_cast<uint32_t>((it >> 1) & 1))) {
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const unsigned char* sp = stages + st * kKpbStageBytes;
-        const unsigned char* vrow = sp + kKpbKBytes + row * 128;
-        const unsigned char* grow = sp + kKpbKBytes + 2 * kKpbAtom + row * 128;
         const float al = live ? a.alpha[(t * a.H + h) * S + s] : 0.f;
         const float cf = live ? a.coef[static_cast<long long>(s) * a.N + t] : 0.f;
-        T* out = static_cast<T*>(a.gv[s]) + t * a.d + c_base;
-#pragma unroll 1
-        for (int c0 = 0; c0 < kKpbCols; c0 += 16) {
-          float dn[16];
-          tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + ab * kKpbCols + c0, dn);
-          const int atom = c0 >> 6;
-          const int j0 = (c0 & 63) >> 3;  // 16-byte chunk inside the 128-byte row
+        const uint32_t sph = static_cast<uint32_t>((it / kKpbStages) & 1);
+        good = good && !*abort_flag && mbar_wait_bounded(&full[st], sph) &&
+               mbar_wait_bounded(&acc_full[ab], static_cast<uint32_t>((it >> 1) & 1)) &&
+               mbar_wait_bounded(&vfree[st], sph);
+        if (!good) *abort_flag = 1;
+        if (good) {
+          tc_fence_after();
+          unsigned char* vrow = stages + st * kKpbStageBytes + kKpbKBytes + half * kKpbAtom + row * 128;
+          const uint32_t tcol = tmem_base + lane_off + ab * kKpbCols + half * kTmaBoxCols;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int sw = ((j0 + hh) ^ (row & 7)) << 4;
-            const Pack<T, 8> vp = *reinterpret_cast<const Pack<T, 8>*>(vrow + atom * kKpbAtom + sw);
-            const Pack<T, 8> gp = *reinterpret_cast<const Pack<T, 8>*>(grow + atom * kKpbAtom + sw);
-            float o[8];
+          for (int c0 = 0; c0 < kTmaBoxCols; c0 += 32) {
+            uint32_t d0[16], d1[16];
+            tmem_ld16_nowait(tcol + c0, d0);
+            tmem_ld16_nowait(tcol + c0 + 16, d1);
+            tmem_ld_wait();
+            tmem_regs_ready(d0);
+            tmem_regs_ready(d1);
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              o[e] = fmaf(al, Elem<T>::to_f(gp.e[e]), dn[hh * 8 + e] - Elem<T>::to_f(vp.e[e]) * cf);
-            if (live) store_pack<T, 8>(out + c0 + hh * 8, o);
+            for (int hh = 0; hh < 4; ++hh) {
+              const int off = (((c0 >> 3) + hh) ^ (row & 7)) << 4;
+              const Pack<T, 8> vp = *reinterpret_cast<const Pack<T, 8>*>(vrow + off);
+              const Pack<T, 8> gp = *reinterpret_cast<const Pack<T, 8>*>(grow + off);
+              float o[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const uint32_t dr = hh < 2 ? d0[hh * 8 + e] : d1[(hh - 2) * 8 + e];
+                o[e] = fmaf(al, Elem<T>::to_f(gp.e[e]), __uint_as_float(dr) - Elem<T>::to_f(vp.e[e]) * cf);
+              }
+              store_pack<T, 8>(reinterpret_cast<T*>(vrow + off), o);
+            }
+          }
+          tc_fence_before();
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&acc_empty[ab]);
+            if (s == S - 1) mbar_arrive(&gempty[gb]);
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&acc_empty[ab]);
-          mbar_arrive(&empty[st]);
-        }
+        // the whole dV tile is in shared memory: hand it to the store warp
+        stopped = consumer_sync_or(kKpbEpiWarps * 32 + 32, !good || *abort_flag != 0);
+        if (stopped) break;
       }
     }
-    // this CTA's slice of dWt: lane = column of the slice, 64 fp32 columns = r
-    float* part = a.partials + (static_cast<long long>(blockIdx.x) * kKpbCols + row) * kKpbR;
+    const bool ok = has_tiles && !stopped;
+    // this CTA's slice of dWt: lane = column of the slice, this warp's 32 of
+    // the 64 fp32 columns (= r)
+    float* part = a.partials + (static_cast<long long>(blockIdx.x) * kKpbCols + row) * kKpbR + half * 32;
     if (ok && mbar_wait_bounded(done, 0)) {
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < kKpbR; c0 += 16) {
+      for (int c0 = 0; c0 < 32; c0 += 16) {
         float v[16];
-        tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + 2 * kKpbCols + c0, v);
+        tmem_ld16(tmem_base + lane_off + 2 * kKpbCols + half * 32 + c0, v);
 #pragma unroll
         for (int e = 0; e < 16; e += 4)
           *reinterpret_cast<float4*>(part + c0 + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
       }
     } else {
       if (has_tiles) atomicOr(&g_kpb_status, kStatusFullWaitTimeout);
-      for (int c0 = 0; c0 < kKpbR; c0 += 4) *reinterpret_cast<float4*>(part + c0) = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c0 = 0; c0 < 32; c0 += 4) *reinterpret_cast<float4*>(part + c0) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   tc_fence_before();
@@ -402,12 +474,14 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
 
   KpbArgs a{};
   bool ok = true;
-  for (int s = 0; s < S && ok; ++s) ok = encode_2d(&a.vmap[s], dtype, values[s], N, d, vstr[s], kKpbRows);
+  for (int s = 0; s < S && ok; ++s) {
+    ok = encode_2d(&a.vmap[s], dtype, values[s], N, d, vstr[s], kKpbRows);
+    ok = ok && encode_2d(&a.gvmap[s], dtype, grad_values[s], N, d, d, kKpbRows);
+  }
   ok = ok && encode_2d(&a.gmap, dtype, g, N, d, d, kKpbRows);
   ok = ok && encode_3d(&a.kmap, dtype, dks, S, N, kKpbR, kKpbRows);
   ok = ok && encode_2d(&a.wtmap, dtype, wt, d, kKpbR, kKpbR, kKpbCols);
   if (!ok) return cudaErrorInvalidValue;
-  for (int s = 0; s < S; ++s) a.gv[s] = grad_values[s];
   a.alpha = alpha;
   a.coef = coef;
   a.partials = partials;
@@ -420,11 +494,11 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
   const uint32_t ab = bf ? 1u : 0u;
   a.idesc_dn = umma_idesc_f16(ab, 0, 0, kKpbRows, kKpbCols);
   a.idesc_dw = umma_idesc_f16(ab, 1, 1, kKpbCols, kKpbR);
-  const size_t smem = 1024 + kKpbKBytes + kKpbStages * kKpbStageBytes + 256;
+  const size_t smem = kKpbSmem;
   auto fn = bf ? keyproj_bwd_tc_kernel<__nv_bfloat16> : keyproj_bwd_tc_kernel<__half>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  fn<<<nch * G, 192, smem, st>>>(a);
+  fn<<<nch * G, kKpbThreads, smem, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int n = kKpbR * d;

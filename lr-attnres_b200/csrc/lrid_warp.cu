@@ -39,8 +39,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Backward warps per CTA: up to 16, or 12 above 16 sources, where the larger
+// per-source register arrays need more registers per thread (and shared memory
+// holds no more warps' rings anyway).
+constexpr int kStreamBwdWarps = 16;
+constexpr int kStreamBwdWarpsManySources = 12;
+
 template <typename T, int KP, int SMAX, bool BWD>
-__global__ void __launch_bounds__(BWD ? 512 : 640, 1) lrid_stream_kernel(const __grid_constant__ LridArgs a) {
+__global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources : kStreamBwdWarps) * 32 : 640, 1) lrid_stream_kernel(const __grid_constant__ LridArgs a) {
   constexpr int VEC = 16 / sizeof(T);
   constexpr int KE = KP * VEC;
   constexpr int CW = 32 * VEC;  // columns per chunk unit (512 bytes per row)
@@ -539,6 +545,8 @@ using WarpFn = void (*)(LridArgs);
 template <typename T, int KP, bool BWD>
 static WarpFn pick_stream_s(int S) {
   if (S <= 16) return lrid_stream_kernel<T, KP, 16, BWD>;
+  if (S <= 20) return lrid_stream_kernel<T, KP, 20, BWD>;
+  if (S <= 24) return lrid_stream_kernel<T, KP, 24, BWD>;
   if (S <= 32) return lrid_stream_kernel<T, KP, 32, BWD>;
   return lrid_stream_kernel<T, KP, 64, BWD>;
 }
@@ -591,7 +599,7 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
   const size_t kcopy_off = align_up(5 * static_cast<size_t>(base.H) * ((base.S + 3) & ~3) * sizeof(float), 16);
   const size_t wscr = align_up(kcopy_off + (bwd ? key_unit : 0), 128);
   const int nsw = std::max(2, std::min(kStreamMaxStages, env_int_w("ATTNRES_STREAM_STAGES", 2)));
-  const int max_warps = bwd ? 16 : 20;
+  const int max_warps = bwd ? (base.S > 16 ? kStreamBwdWarpsManySources : kStreamBwdWarps) : 20;
   int nw = std::min(max_warps, std::max(1, env_int_w("ATTNRES_STREAM_WARPS", max_warps)));
   for (; nw >= 1; --nw) {
     size_t off = kStreamMaxWarps * kStreamMaxStages * (sizeof(uint64_t) + sizeof(long long)) +
