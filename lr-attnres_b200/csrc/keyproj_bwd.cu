@@ -9,7 +9,8 @@
 // read backward runs without writing dV and each dV row is written once.
 //
 // Kernels:
-//   * kpb_prepass_kernel: dKs (dtype [S][N][64]) and coef (f32 [S][N]);
+//   * kpb_prepass_kernel: dKs (dtype [S][N][64]) and {alpha, coef} (f32 pairs
+//     [S][H][N]);
 //   * kpb_transpose_w_kernel: Wt = W^T (dtype [d][64]);
 //   * keyproj_bwd_tc_kernel, persistent, one 128-column slice of d per CTA.
 //     The CTA walks its token tiles (128 tokens) and, inside each, the S
@@ -66,8 +67,7 @@ struct KpbArgs {
   CUtensorMap gmap;                   // g as [N, d]
   CUtensorMap kmap;                   // dKs as [S][N][64]
   CUtensorMap wtmap;                  // Wt as [d, 64]
-  const float* alpha;                 // [N][H][S]
-  const float* coef;                  // [S][N]
+  const float2* ac;                   // [S][H][N]: {alpha, coef}
   float* partials;                    // [grid][128][64]
   long long N;
   int S, d, H, nch, ntt;
@@ -265,11 +265,15 @@ __global__ void __launch_bounds__(kKpbThreads, 1) keyproj_bwd_tc_kernel(const __
       bool good = !*abort_flag && mbar_wait_bounded(&gfull[gb], static_cast<uint32_t>((k >> 1) & 1));
       if (!good) *abort_flag = 1;
       const unsigned char* grow = gbuf + gb * kKpbGBytes + half * kKpbAtom + row * 128;
+      const float2* acp = a.ac + static_cast<long long>(h) * a.N + (live ? t : 0);
+      const long long acs = static_cast<long long>(a.H) * a.N;  // next source
+      float2 acn = *acp;                                          // {alpha, coef} of source 0
       for (int s = 0; s < S; ++s, ++it) {
         const int st = static_cast<int>(it % kKpbStages);
         const int ab = static_cast<int>(it & 1);
-        const float al = live ? a.alpha[(t * a.H + h) * S + s] : 0.f;
-        const float cf = live ? a.coef[static_cast<long long>(s) * a.N + t] : 0.f;
+        const float al = live ? acn.x : 0.f;
+        const float cf = live ? acn.y : 0.f;
+        if (s + 1 < S) acn = acp[(s + 1) * acs];  // one tile ahead
         const uint32_t sph = static_cast<uint32_t>((it / kKpbStages) & 1);
         good = good && !*abort_flag && mbar_wait_bounded(&full[st], sph) &&
                mbar_wait_bounded(&acc_full[ab], static_cast<uint32_t>((it >> 1) & 1)) &&
@@ -279,27 +283,24 @@ __global__ void __launch_bounds__(kKpbThreads, 1) keyproj_bwd_tc_kernel(const __
           tc_fence_after();
           unsigned char* vrow = stages + st * kKpbStageBytes + kKpbKBytes + half * kKpbAtom + row * 128;
           const uint32_t tcol = tmem_base + lane_off + ab * kKpbCols + half * kTmaBoxCols;
+          // the thread's 64 dn columns: four TMEM loads, one wait
+          uint32_t dr[4][16];
 #pragma unroll
-          for (int c0 = 0; c0 < kTmaBoxCols; c0 += 32) {
-            uint32_t d0[16], d1[16];
-            tmem_ld16_nowait(tcol + c0, d0);
-            tmem_ld16_nowait(tcol + c0 + 16, d1);
-            tmem_ld_wait();
-            tmem_regs_ready(d0);
-            tmem_regs_ready(d1);
+          for (int j = 0; j < 4; ++j) tmem_ld16_nowait(tcol + 16 * j, dr[j]);
+          tmem_ld_wait();
 #pragma unroll
-            for (int hh = 0; hh < 4; ++hh) {
-              const int off = (((c0 >> 3) + hh) ^ (row & 7)) << 4;
-              const Pack<T, 8> vp = *reinterpret_cast<const Pack<T, 8>*>(vrow + off);
-              const Pack<T, 8> gp = *reinterpret_cast<const Pack<T, 8>*>(grow + off);
-              float o[8];
+          for (int j = 0; j < 4; ++j) tmem_regs_ready(dr[j]);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const uint32_t dr = hh < 2 ? d0[hh * 8 + e] : d1[(hh - 2) * 8 + e];
-                o[e] = fmaf(al, Elem<T>::to_f(gp.e[e]), __uint_as_float(dr) - Elem<T>::to_f(vp.e[e]) * cf);
-              }
-              store_pack<T, 8>(reinterpret_cast<T*>(vrow + off), o);
-            }
+          for (int hh = 0; hh < 8; ++hh) {
+            const int off = (hh ^ (row & 7)) << 4;
+            const Pack<T, 8> vp = *reinterpret_cast<const Pack<T, 8>*>(vrow + off);
+            const Pack<T, 8> gp = *reinterpret_cast<const Pack<T, 8>*>(grow + off);
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              o[e] = fmaf(al, Elem<T>::to_f(gp.e[e]),
+                          __uint_as_float(dr[hh >> 1][(hh & 1) * 8 + e]) - Elem<T>::to_f(vp.e[e]) * cf);
+            store_pack<T, 8>(reinterpret_cast<T*>(vrow + off), o);
           }
           tc_fence_before();
           fence_async_shared();
@@ -342,15 +343,18 @@ __global__ void __launch_bounds__(kKpbThreads, 1) keyproj_bwd_tc_kernel(const __
 }
 
 // dKs = inv * dK (rounded to T) and coef = inv * <inv * dK, k> / d, with
-// eight lanes per (source, token) row of 64 (one 16-byte pack each).
+// eight lanes per (source, token) row of 64 (one 16-byte pack each); the
+// softmax weight is copied next to coef in source-major order, so the fused
+// kernel's epilogue reads one coalesced {alpha, coef} pair per row and tile.
 struct KpbPrepArgs {
   const void* dk[kKpbMaxSources];  // [N, 64] dense per source
   const void* keys;                // [S][N][64]
   const float* inv_rms;            // [S][N], or null without the value norm
+  const float* alpha;              // [N][H][S] softmax weights of the forward
   void* dks;                       // [S][N][64]
-  float* coef;                     // [S][N]
+  float2* ac;                      // [S][H][N]: {alpha, coef}
   long long N;
-  int S, d;
+  int S, d, H;
 };
 
 template <typename T>
@@ -376,7 +380,9 @@ __global__ void __launch_bounds__(256) kpb_prepass_kernel(const __grid_constant_
   c += __shfl_xor_sync(0xffffffffu, c, 4);
   if (!live) return;
   store_pack<T, 8>(static_cast<T*>(a.dks) + r * kKpbR + sub * 8, o);
-  if (sub == 0) a.coef[r] = a.inv_rms ? inv * c / a.d : 0.f;
+  const float cf = a.inv_rms ? inv * c / a.d : 0.f;
+  for (int h = sub; h < a.H; h += 8)
+    a.ac[(static_cast<long long>(s) * a.H + h) * a.N + t] = make_float2(a.alpha[(t * a.H + h) * a.S + s], cf);
 }
 
 // Wt[c][r] = W[r][c]; W is [64, d] with a row stride.
@@ -424,7 +430,7 @@ size_t keyproj_bwd_tc_workspace(int S, long long N, int d, int R, int H, int dty
   int nch, G, ntt;
   if (!kpb_shape(S, N, d, R, H, dtype, &nch, &G, &ntt)) return 0;
   return align256(static_cast<size_t>(d) * kKpbR * 2) + align256(static_cast<size_t>(S) * N * kKpbR * 2) +
-         align256(static_cast<size_t>(S) * N * 4) + align256(static_cast<size_t>(nch) * G * kKpbCols * kKpbR * 4);
+         align256(static_cast<size_t>(S) * H * N * 8) + align256(static_cast<size_t>(nch) * G * kKpbCols * kKpbR * 4);
 }
 
 cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int dtype, const void* const* values,
@@ -440,8 +446,8 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
   ws += align256(static_cast<size_t>(d) * kKpbR * 2);
   void* dks = ws;
   ws += align256(static_cast<size_t>(S) * N * kKpbR * 2);
-  float* coef = reinterpret_cast<float*>(ws);
-  ws += align256(static_cast<size_t>(S) * N * 4);
+  float2* ac = reinterpret_cast<float2*>(ws);
+  ws += align256(static_cast<size_t>(S) * H * N * 8);
   float* partials = reinterpret_cast<float*>(ws);
   const bool bf = dtype == ATTNRES_DTYPE_BF16;
 
@@ -459,11 +465,13 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
     for (int s = 0; s < S; ++s) p.dk[s] = grad_keys[s];
     p.keys = keys;
     p.inv_rms = value_norm ? inv_rms : nullptr;
+    p.alpha = alpha;
     p.dks = dks;
-    p.coef = coef;
+    p.ac = ac;
     p.N = N;
     p.S = S;
     p.d = d;
+    p.H = H;
     const long long threads = static_cast<long long>(S) * N * 8;
     const unsigned pg = static_cast<unsigned>((threads + 255) / 256);
     if (bf) kpb_prepass_kernel<__nv_bfloat16><<<pg, 256, 0, st>>>(p);
@@ -482,8 +490,7 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
   ok = ok && encode_3d(&a.kmap, dtype, dks, S, N, kKpbR, kKpbRows);
   ok = ok && encode_2d(&a.wtmap, dtype, wt, d, kKpbR, kKpbR, kKpbCols);
   if (!ok) return cudaErrorInvalidValue;
-  a.alpha = alpha;
-  a.coef = coef;
+  a.ac = ac;
   a.partials = partials;
   a.N = N;
   a.S = S;
