@@ -41,6 +41,8 @@ CONFIGS = {
     "config4": dict(S=17, B=32, T=4096, D=2048, R=64, H=1, scale=1 / 8, query="static", kv=True),
     # small case for ncu captures (inputs still > L2)
     "small": dict(S=9, B=4, T=2048, D=1024, R=64, H=1, scale=1 / 8, query="static"),
+    # config-4 shapes at 8192 tokens for ncu captures of the key-from-value kernels (570 MB of values)
+    "small_kv": dict(S=17, B=2, T=4096, D=2048, R=64, H=1, scale=1 / 8, query="static", kv=True),
 }
 
 
@@ -285,6 +287,11 @@ def main():
 
     from attnres_b200.sharding import allreduce_param_grads
 
+    def allreduce(dq, dgate):
+        # the only cross-GPU step: one bucketed NCCL all-reduce of the summed grads
+        if world > 1:
+            allreduce_param_grads([dq] + ([dgate] if gated else []) + ([dw] if kv else []))
+
     stream = torch.cuda.Stream(device)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
 
@@ -297,78 +304,76 @@ def main():
             print(json.dumps({"profile_run": True, "config": args.config}), flush=True)
         return
 
-    # ---- the training step as CUDA graphs ---------------------------------
-    # One step = forward, backward and (N > 1) the gradient all-reduce. The
-    # all-reduce of step k runs on its own stream, overlapping the forward of
-    # step k+1 (which does not read it); the backward of step k+1 waits for it
-    # before its buffers can be reused. Warm-up replays a one-step graph W
-    # times; the timed region is ONE replay of a graph holding the K steps, with
-    # external timing events around each step's forward and backward kernels,
-    # so no host launch gap sits between the kernels of the timed region.
+    # ---- capture fwd and bwd as two CUDA graphs (static buffers) ----------
     with torch.cuda.stream(stream):
         for _ in range(3):  # allocator warm-up outside capture
-            bwd(*fwd())
+            res = bwd(*fwd())
     torch.cuda.synchronize()
-    comm = torch.cuda.Stream(device)
-
-    def capture_steps(n, events=None):
-        prev = None
-        for i in range(n):
-            if events:
-                events[i][0].record(stream)
-            fo = fwd()
-            if events:
-                events[i][1].record(stream)
-            if prev is not None and world > 1:
-                stream.wait_event(prev[1])
-            if events:
-                events[i][2].record(stream)
-            res = bwd(*fo)
-            if events:
-                events[i][3].record(stream)
-            del fo
-            done = None
-            if world > 1:
-                bwd_done = torch.cuda.Event()
-                bwd_done.record(stream)
-                comm.wait_event(bwd_done)
-                with torch.cuda.stream(comm):
-                    allreduce_param_grads([res[2]] + ([res[3]] if gated else []) + ([res[1]] if kv else []))
-                    done = torch.cuda.Event()
-                    done.record(comm)
-            prev = (res, done)
-        if world > 1:
-            stream.wait_event(prev[1])  # join the side stream before the capture ends
-        return prev[0]
-
-    g_one, g_all = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_one, stream=stream):
-        capture_steps(1)
-    step_events = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
-                   for _ in range(args.steps)]
-    with torch.cuda.graph(g_all, stream=stream):
-        capture_steps(args.steps, step_events)
+    g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_fwd, stream=stream):
+        fo = fwd()
+    with torch.cuda.graph(g_bwd, stream=stream):
+        res = bwd(*fo)
+    dq, dgate = res[2], res[3]
+    dw = res[1] if kv else None
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
     sampler.start()
+    # The gradient all-reduce of step k runs on its own stream, overlapping the
+    # forward of step k+1 (which does not read it); the backward of step k+1,
+    # which rewrites the gradient buffers, waits for it.
+    comm = torch.cuda.Stream(device)
+    bwd_done = [torch.cuda.Event() for _ in range(2)]
+    comm_done = [torch.cuda.Event() for _ in range(2)]
+
+    def step(i, fe=None, be=None):
+        if fe:
+            fe[0].record(stream)
+        g_fwd.replay()
+        if fe:
+            fe[1].record(stream)
+        if world > 1 and i > 0:
+            stream.wait_event(comm_done[(i - 1) % 2])
+        if be:
+            be[0].record(stream)
+        g_bwd.replay()
+        if be:
+            be[1].record(stream)
+        if world > 1:
+            bwd_done[i % 2].record(stream)
+            comm.wait_event(bwd_done[i % 2])
+            with torch.cuda.stream(comm):
+                allreduce(dq, dgate)
+                comm_done[i % 2].record(comm)
+
+    def drain(last):
+        if world > 1:
+            stream.wait_event(comm_done[last % 2])
+
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            g_one.replay()
+        for i in range(args.warmup):
+            step(i)
+        drain(args.warmup - 1)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    # per-kernel CUDA-event timing on the launching stream
+    fwd_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+    bwd_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
     with torch.cuda.stream(stream):
         ev[0].record(stream)
-        g_all.replay()
+        for i in range(args.steps):
+            step(i, fwd_events[i], bwd_events[i])
+        drain(args.steps - 1)
         ev[1].record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    fwd_events = [(e[0], e[1]) for e in step_events]
-    bwd_events = [(e[2], e[3]) for e in step_events]
     ms = ev[0].elapsed_time(ev[1]) / args.steps
     fwd_ms = float(np.mean([a.elapsed_time(b) for a, b in fwd_events]))
     bwd_ms = float(np.mean([a.elapsed_time(b) for a, b in bwd_events]))
