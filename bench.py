@@ -430,6 +430,36 @@ def main():
                 "peak_tflops": tpeak, "frac_tensor": flops / pms / 1e9 / tpeak,
                 "gbs": pbytes / pms / 1e6, "frac_hbm": pbytes / pms / 1e6 / hbm}
 
+    # a9: the block-summary op (running block sum + scaled source) on rows of
+    # this config, 4x its token count so the four arrays (537 MB at config 2)
+    # are far larger than L2
+    aux = None
+    if not kv:
+        xs = torch.randn(4 * c["B"], c["T"], c["D"], device=device, dtype=torch.bfloat16)
+        ps = torch.randn_like(xs)
+        bsum = torch.ops.attnres.block_summary
+        with torch.cuda.stream(stream):
+            bsum(ps, xs, None, 0.25)
+        torch.cuda.synchronize()
+        g_sum = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_sum, stream=stream):
+            bsum(ps, xs, None, 0.25)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g_sum.replay()
+            s0.record(stream)
+            for _ in range(20):
+                g_sum.replay()
+            s1.record(stream)
+        torch.cuda.synchronize()
+        sms = s0.elapsed_time(s1) / 20
+        sbytes = 4 * xs.numel() * 2
+        aux = {"block_summary": {"kernel": "summary_fwd_kernel (a9: sum = partial + x, source = sum * c)",
+                                 "elements": xs.numel(), "ms": sms, "achieved_gbs": sbytes / sms / 1e6,
+                                 "frac": sbytes / sms / 1e6 / hbm, "bytes": sbytes}}
+        del xs, ps
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not kv:
         r, cores, sample = cpu_oracle_rate(c, target_s=12.0)
@@ -459,6 +489,7 @@ def main():
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
+            "aux": aux,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

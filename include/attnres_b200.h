@@ -241,6 +241,31 @@ int attnres_lrid_key_projection_backward_tc(int num_sources, int64_t num_tokens,
                                             void* stream);
 
 /*
+ * Block summary of block Attention Residuals, one pass over the rows:
+ *   sum = partial + x (partial may be NULL),  source = sum * c
+ * with c = *scale_device when scale_device is not NULL (a learned scale,
+ * already in the value dtype's precision), else `scale` (count^-alpha).
+ * sum may be NULL when only the source is wanted. dtype arrays of
+ * num_elements elements. Replaces the running sum and the
+ * _attnres_block_summary / _lrid_block_source value scaling of
+ * model.py:990-1028 (call sites model.py:2377-2389, :2451-2463).
+ */
+int attnres_block_summary_forward(int64_t num_elements, int dtype, const void* partial, const void* x,
+                                  const float* scale_device, float scale, void* sum, void* source,
+                                  void* stream);
+/*
+ * Backward: grad_partial (the gradient of both partial and x) =
+ * round(round(grad_source * c) + grad_sum); either input may be NULL. With
+ * grad_scale (float, one element) the scale gradient sum(grad_source * sum)
+ * is reduced deterministically using a workspace of
+ * attnres_block_summary_backward_workspace_bytes(num_elements) bytes.
+ */
+size_t attnres_block_summary_backward_workspace_bytes(int64_t num_elements);
+int attnres_block_summary_backward(int64_t num_elements, int dtype, const void* grad_source, const void* grad_sum,
+                                   const void* sum, const float* scale_device, float scale, void* grad_partial,
+                                   float* grad_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Cached-logit block read ("phase 1"): Q reads of the same S sources whose
  * logits were computed once. Replaces attention_residual_phase1_from_logits
  * (attnres_ops.py:3910-3961) and its Triton kernels (:933-989, :1069-1140).

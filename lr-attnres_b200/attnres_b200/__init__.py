@@ -8,7 +8,9 @@ public read functions.
 """
 from . import _native
 from .ops import (
+    attention_residual_block_summary,
     attention_residual_read,
+    block_summary,
     base_read,
     is_fused_attnres_available,
     lrid_attention_residual_read,
@@ -22,7 +24,9 @@ from .ops import (
 )
 
 __all__ = [
+    "attention_residual_block_summary",
     "attention_residual_read",
+    "block_summary",
     "base_read",
     "is_fused_attnres_available",
     "lrid_attention_residual_read",

@@ -37,6 +37,9 @@ EXPORTED_SYMBOLS = (
     "attnres_lrid_key_projection_backward",
     "attnres_lrid_key_projection_backward_tc_workspace_bytes",
     "attnres_lrid_key_projection_backward_tc",
+    "attnres_block_summary_forward",
+    "attnres_block_summary_backward_workspace_bytes",
+    "attnres_block_summary_backward",
     "attnres_phase1_forward",
     "attnres_phase1_backward",
     "attnres_noalloc_scratch_bytes",
@@ -113,6 +116,12 @@ def load(path=None):
         PP, P, P, SZ,                # grad_values, grad_weight, workspace, workspace bytes
         P,                           # stream
     ]
+    L.attnres_block_summary_forward.restype = I
+    L.attnres_block_summary_forward.argtypes = [I64, I, P, P, P, F, P, P, P]
+    L.attnres_block_summary_backward_workspace_bytes.restype = SZ
+    L.attnres_block_summary_backward_workspace_bytes.argtypes = [I64]
+    L.attnres_block_summary_backward.restype = I
+    L.attnres_block_summary_backward.argtypes = [I64, I, P, P, P, P, F, P, P, P, SZ, P]
     L.attnres_phase1_forward.restype = I
     L.attnres_phase1_forward.argtypes = [I, I, I64, I, I, PP, PI64, P, I, I, F, P, P, P, P]
     L.attnres_phase1_backward.restype = I

@@ -1049,3 +1049,100 @@ def attention_residual_average_read(values, normalize_output: bool = False, forc
     q = torch.zeros(values[0].size(-1), device=values[0].device, dtype=values[0].dtype)
     out, _ = base_read(values, q, None, False, bool(normalize_output))
     return out
+
+
+# ---------------------------------------------------------------------------
+# attnres::block_summary — running block sum and scaled block source (one pass)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("attnres::block_summary", mutates_args=())
+def block_summary(partial: Optional[Tensor], x: Tensor, scale: Optional[Tensor],
+                  scale_value: float) -> tuple[Tensor, Tensor]:
+    """sum = partial + x (partial None: sum = x), source = sum * c with c the
+    device scalar `scale` (fp32, one element) when given, else `scale_value`."""
+    _require_cuda([partial, x, scale], "block summary inputs")
+    dtype = x.dtype
+    xc = x.contiguous()
+    pc = None if partial is None else partial.to(dtype).contiguous()
+    if pc is not None and pc.shape != xc.shape:
+        raise RuntimeError("attnres_b200: block summary partial and x must have one shape")
+    sc = None if scale is None else scale.to(torch.float32).reshape(1).contiguous()
+    out_sum = torch.empty_like(xc)
+    src = torch.empty_like(xc)
+    with torch.cuda.device(x.device):
+        rc = N.load().attnres_block_summary_forward(
+            xc.numel(), _dtype_code(dtype), _ptr(pc), _ptr(xc), _ptr(sc), float(scale_value), _ptr(out_sum),
+            _ptr(src), _stream_ptr(x.device))
+    N.check(rc, "attnres_block_summary_forward")
+    return out_sum, src
+
+
+@block_summary.register_fake
+def _(partial, x, scale, scale_value):
+    return x.new_empty(x.shape), x.new_empty(x.shape)
+
+
+@torch.library.custom_op("attnres::block_summary_backward", mutates_args=())
+def block_summary_backward(grad_source: Optional[Tensor], grad_sum: Optional[Tensor], out_sum: Tensor,
+                           scale: Optional[Tensor], scale_value: float, want_scale_grad: bool) -> tuple[Tensor, Tensor]:
+    """Returns (gradient of partial and of x, scale gradient [1] fp32 or empty)."""
+    dtype = out_sum.dtype
+    gs = None if grad_source is None else grad_source.to(dtype).contiguous()
+    gm = None if grad_sum is None else grad_sum.to(dtype).contiguous()
+    sc = None if scale is None else scale.to(torch.float32).reshape(1).contiguous()
+    n = out_sum.numel()
+    g = torch.empty_like(out_sum)
+    dsc = torch.empty((1,) if want_scale_grad else (0,), device=out_sum.device, dtype=torch.float32)
+    L = N.load()
+    ws_bytes = L.attnres_block_summary_backward_workspace_bytes(n) if want_scale_grad else 0
+    ws = torch.empty((max(ws_bytes, 1),), device=out_sum.device, dtype=torch.uint8)
+    with torch.cuda.device(out_sum.device):
+        rc = L.attnres_block_summary_backward(
+            n, _dtype_code(dtype), _ptr(gs), _ptr(gm), _ptr(out_sum), _ptr(sc), float(scale_value), _ptr(g),
+            _ptr(dsc) if want_scale_grad else None, _ptr(ws), ws_bytes, _stream_ptr(out_sum.device))
+    N.check(rc, "attnres_block_summary_backward")
+    return g, dsc
+
+
+@block_summary_backward.register_fake
+def _(grad_source, grad_sum, out_sum, scale, scale_value, want_scale_grad):
+    return out_sum.new_empty(out_sum.shape), out_sum.new_empty((1,) if want_scale_grad else (0,),
+                                                               dtype=torch.float32)
+
+
+def _block_summary_setup(ctx, inputs, output):
+    partial, x, scale, scale_value = inputs
+    out_sum, _ = output
+    ctx.has_partial = partial is not None
+    ctx.scale_value = float(scale_value)
+    ctx.scale_shape = None if scale is None else scale.shape
+    ctx.scale_dtype = None if scale is None else scale.dtype
+    ctx.save_for_backward(out_sum, scale)
+
+
+def _block_summary_bwd(ctx, grad_sum, grad_source):
+    out_sum, scale = ctx.saved_tensors
+    want = scale is not None and ctx.needs_input_grad[2]
+    g, dsc = block_summary_backward(grad_source, grad_sum, out_sum, scale, ctx.scale_value, want)
+    dscale = dsc.reshape(ctx.scale_shape).to(ctx.scale_dtype) if want else None
+    return (g if ctx.has_partial else None, g, dscale, None)
+
+
+block_summary.register_autograd(_block_summary_bwd, setup_context=_block_summary_setup)
+
+
+def attention_residual_block_summary(partial_block: Optional[Tensor], layer_output: Tensor, count: int = 1,
+                                     alpha=1.0, scale: Optional[Tensor] = None):
+    """The running block sum and the scaled block source of block Attention
+    Residuals in one pass: returns (partial_block + layer_output,
+    (partial_block + layer_output) * c). c is the learned `scale` (cast to the
+    value dtype, as model.py:978-983 does), else count ** -alpha with alpha a
+    float or a tensor (model.py:955-959; a tensor alpha keeps its gradient).
+    Replaces the add and the multiply of model.py:2377-2389 / :990-1001; the
+    same call scales key sums (model.py:1011-1016)."""
+    dtype = layer_output.dtype
+    if scale is not None:
+        return block_summary(partial_block, layer_output, scale.to(dtype), 1.0)
+    if torch.is_tensor(alpha):
+        c = torch.exp(-alpha * alpha.new_tensor(float(count)).log())
+        return block_summary(partial_block, layer_output, c.to(dtype), 1.0)
+    return block_summary(partial_block, layer_output, None, float(count) ** (-float(alpha)))

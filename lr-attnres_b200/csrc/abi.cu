@@ -518,6 +518,42 @@ int attnres_lrid_key_projection_backward_tc(int num_sources, int64_t num_tokens,
   return ATTNRES_OK;
 }
 
+int attnres_block_summary_forward(int64_t num_elements, int dtype, const void* partial, const void* x,
+                                  const float* scale_device, float scale, void* sum, void* source,
+                                  void* stream) {
+  if (num_elements < 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "num_elements < 0");
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (num_elements > 0 && (!x || !source)) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary: NULL x/source");
+  cudaError_t e = attnres::summary_forward_launch(num_elements, dtype, partial, x, scale_device, scale, sum, source,
+                                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_block_summary_forward launch");
+  return ATTNRES_OK;
+}
+
+size_t attnres_block_summary_backward_workspace_bytes(int64_t num_elements) {
+  if (num_elements <= 0) return 0;
+  return sizeof(float) * static_cast<size_t>(attnres::summary_bwd_grid(num_elements));
+}
+
+int attnres_block_summary_backward(int64_t num_elements, int dtype, const void* grad_source, const void* grad_sum,
+                                   const void* sum, const float* scale_device, float scale, void* grad_partial,
+                                   float* grad_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_elements < 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "num_elements < 0");
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (num_elements > 0 && !grad_partial) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary: NULL grad_partial");
+  const bool want_dc = grad_scale && grad_source && num_elements > 0;
+  if (want_dc) {
+    if (!sum) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary: the scale gradient needs the saved sum");
+    if (!workspace || workspace_bytes < attnres_block_summary_backward_workspace_bytes(num_elements))
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary: workspace too small");
+  }
+  cudaError_t e = attnres::summary_backward_launch(num_elements, dtype, grad_source, grad_sum, sum, scale_device,
+                                                   scale, grad_partial, grad_scale, static_cast<float*>(workspace),
+                                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_block_summary_backward launch");
+  return ATTNRES_OK;
+}
+
 int attnres_phase1_forward(int num_sources, int num_queries, int64_t num_tokens, int value_dim, int dtype,
                            const void* const* values, const int64_t* value_row_strides, const void* logits,
                            int logit_dtype, int output_norm, float output_eps, void* output, float* lse,

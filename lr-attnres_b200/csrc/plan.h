@@ -167,6 +167,15 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
                                   const void* g, const float* alpha, int value_norm, void* const* grad_values,
                                   float* grad_weight, void* workspace, size_t workspace_bytes, cudaStream_t st);
 cudaError_t read_keyproj_bwd_status(unsigned* status, bool reset);
+
+// Block summary (summary.cu).
+int summary_bwd_grid(long long n);
+cudaError_t summary_forward_launch(long long n, int dtype, const void* partial, const void* x,
+                                   const float* scale_dev, float scale, void* sum, void* source,
+                                   cudaStream_t st);
+cudaError_t summary_backward_launch(long long n, int dtype, const void* g_source, const void* g_sum,
+                                    const void* sum, const float* scale_dev, float scale, void* g_total,
+                                    float* grad_scale, float* partials, cudaStream_t st);
 }  // namespace attnres
 
 namespace attnres {
