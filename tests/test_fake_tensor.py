@@ -35,3 +35,7 @@ def test_fake_shapes_of_all_ops():
         assert po.shape == (Q, B, T, D) and lse.shape == (Q, B, T)
         bo, binv = ops.base_read(v, _fake(mode, D), None, True, True)
         assert bo.shape == (B, T, D) and binv.shape == (B * T,)
+        ssum, ssrc = ops.block_summary(v[0], v[1], None, 0.5)
+        assert ssum.shape == (B, T, D) and ssrc.shape == (B, T, D)
+        gp, gsc = ops.block_summary_backward(g, None, ssum, _fake(mode, 1, dtype=torch.float32), 1.0, True)
+        assert gp.shape == (B, T, D) and gsc.shape == (1,)
