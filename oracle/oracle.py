@@ -220,3 +220,78 @@ def phase1_backward(values, logits, grad_output, grad_lse=None, normalize_output
     if grad_lse is not None:
         dl = dl + np.asarray(grad_lse, np.float64)[:, None, :] * alpha
     return {"dV": dV, "dlogits": dl}
+
+
+PHASE2_LRID, PHASE2_BASE, PHASE2_LOGIT = 0, 1, 2
+
+
+def phase2_forward(mode, partial_value, interblock_output, interblock_lse, partial_key=None, query=None,
+                   partial_logit=None, logit_scale=1.0, key_norm=False, key_eps=float(np.finfo(np.float32).eps),
+                   logit_bias=0.0, normalize_output=False, output_eps=float(np.finfo(np.float32).eps)):
+    """Cached-logit phase 2, double precision: the live partial block merged into
+    the phase-1 result (attnres_ops.py:4142-4160 for LRID keys, :2630-2642 for
+    the base key rms_norm(partial_value), :4043-4072 given the logit):
+      logit = scale <k_hat, q> + bias (or the given logit), p = sigmoid(logit - lse)
+      merged = prev + p (v - prev),   out = merged (* rms inv when normalized).
+    partial_value / interblock_output [N, d], interblock_lse [N], partial_key
+    [N, R], query [R] (LRID) or [d] (base), partial_logit [N]."""
+    v = np.asarray(partial_value, np.float64)
+    prev = np.asarray(interblock_output, np.float64)
+    lse = np.asarray(interblock_lse, np.float64)
+    kinv = None
+    khat = None
+    if mode == PHASE2_LOGIT:
+        logit = np.asarray(partial_logit, np.float64).copy()
+    else:
+        k = np.asarray(partial_key if mode == PHASE2_LRID else partial_value, np.float64)
+        q = np.asarray(query, np.float64).reshape(-1)
+        kinv = 1.0 / np.sqrt((k * k).mean(-1) + key_eps) if key_norm else np.ones(k.shape[0])
+        khat = k * kinv[:, None]
+        logit = (khat @ q) * (logit_scale if mode == PHASE2_LRID else 1.0)
+    logit = logit + float(logit_bias)
+    p = 1.0 / (1.0 + np.exp(-(logit - lse)))
+    merged = prev + p[:, None] * (v - prev)
+    inv = None
+    out = merged
+    if normalize_output:
+        inv = 1.0 / np.sqrt((merged * merged).mean(-1) + output_eps)
+        out = merged * inv[:, None]
+    return out, {"p": p, "merged": merged, "inv": inv, "kinv": kinv, "khat": khat}
+
+
+def phase2_backward(mode, partial_value, interblock_output, interblock_lse, grad_output, partial_key=None,
+                    query=None, partial_logit=None, logit_scale=1.0, key_norm=False,
+                    key_eps=float(np.finfo(np.float32).eps), logit_bias=0.0, normalize_output=False,
+                    output_eps=float(np.finfo(np.float32).eps)):
+    """Analytic gradients of phase2_forward (the reference's backward kernel
+    attnres_ops.py:2058-2121 and the autograd of its PyTorch path)."""
+    v = np.asarray(partial_value, np.float64)
+    prev = np.asarray(interblock_output, np.float64)
+    out, st = phase2_forward(mode, partial_value, interblock_output, interblock_lse, partial_key, query,
+                             partial_logit, logit_scale, key_norm, key_eps, logit_bias, normalize_output,
+                             output_eps)
+    g = np.asarray(grad_output, np.float64)
+    if normalize_output:
+        y = out
+        g = st["inv"][:, None] * (g - y * (g * y).mean(-1, keepdims=True))
+    p = st["p"]
+    dl = p * (1.0 - p) * (g * (v - prev)).sum(-1)
+    res = {"d_partial_value": p[:, None] * g, "d_interblock_output": (1.0 - p)[:, None] * g,
+           "d_interblock_lse": -dl, "dbias": dl.sum()}
+    if mode == PHASE2_LOGIT:
+        res["d_partial_logit"] = dl
+        return res
+    q = np.asarray(query, np.float64).reshape(-1)
+    sc = logit_scale if mode == PHASE2_LRID else 1.0
+    khat, kinv = st["khat"], st["kinv"]
+    dkhat = (dl * sc)[:, None] * q[None, :]
+    if key_norm:
+        dk = kinv[:, None] * (dkhat - khat * (dkhat * khat).mean(-1, keepdims=True))
+    else:
+        dk = dkhat
+    res["dq"] = ((dl * sc)[:, None] * khat).sum(0)
+    if mode == PHASE2_LRID:
+        res["d_partial_key"] = dk
+    else:
+        res["d_partial_value"] = res["d_partial_value"] + dk
+    return res

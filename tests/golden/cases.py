@@ -41,6 +41,16 @@ CASES = [
     # cached-logit block read (attention_residual_phase1_from_logits, attnres_ops.py:3910)
     dict(name="phase1_q3", kind="phase1", S=5, Q=3, B=2, T=6, D=64, seed=41),
     dict(name="phase1_q2_norm", kind="phase1", S=4, Q=2, B=1, T=9, D=32, normalize_output=True, seed=42),
+    # cached-logit phase 2: merge of the live partial block (attnres_ops.py:3964-4160)
+    dict(name="phase2_lrid", kind="phase2", mode="lrid", S=1, B=2, T=7, D=48, R=16, scale=0.25, key_norm=True,
+         seed=51),
+    dict(name="phase2_lrid_bias_norm", kind="phase2", mode="lrid", S=1, B=1, T=9, D=64, R=32, scale=0.5,
+         key_norm=False, bias=True, normalize_output=True, seed=52),
+    dict(name="phase2_base", kind="phase2", mode="base", S=1, B=2, T=5, D=32, key_norm=True, seed=53),
+    dict(name="phase2_base_bias_raw", kind="phase2", mode="base", S=1, B=1, T=8, D=40, key_norm=False, bias=True,
+         query_std=0.1, seed=54),
+    dict(name="phase2_logit_norm", kind="phase2", mode="logit", S=1, B=2, T=6, D=24, normalize_output=True,
+         seed=55),
     # base AttnRes read, mirrors test_fused_base_attnres_matches_torch (:884-895)
     dict(name="base_small_kn", kind="base", S=5, B=2, T=5, D=64, key_norm=True, seed=21),
     dict(name="base_small_nokn", kind="base", S=5, B=2, T=5, D=64, key_norm=False, seed=22),
@@ -63,6 +73,17 @@ def case_inputs(case):
         inp["query"] = f(H, R // H)
         inp["query_dynamic"] = f(N, H, R // H)
         inp["gate"] = (0.1 + 0.2 * rng.standard_normal(H)).astype(np.float32)
+    elif case["kind"] == "phase2":
+        inp = {"partial_value": f(N, D), "interblock_output": f(N, D), "interblock_lse": f(N),
+               "grad_output": f(N, D), "logit_bias": np.float32(rng.standard_normal())}
+        if case["mode"] == "lrid":
+            inp["partial_key"] = f(N, case["R"])
+            inp["query"] = f(case["R"])
+        elif case["mode"] == "base":
+            inp["query"] = (f(D) * np.float32(case.get("query_std", 1.0))).astype(np.float32)
+        else:
+            inp["partial_logit"] = f(N)
+        return inp
     elif case["kind"] == "phase1":
         inp["logits"] = f(case["Q"], S, N)
         inp["grad_lse"] = f(case["Q"], N)

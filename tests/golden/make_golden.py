@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
 Run (in a container where the reference checkout is available):
-    ATTNRES_REFERENCE=/path/to/LR-AttnRes python tests/golden/make_golden.py
+    ATTNRES_REFERENCE=/path/to/LR-AttnRes python tests/golden/make_golden.py [case-name-prefix ...]
 
 It imports the reference's attnres_ops.py and runs its public read functions on
 CPU fp32 tensors, which routes them through the reference's unfused PyTorch path
@@ -40,9 +40,43 @@ def run_case(ref, case):
     kind = case["kind"]
     B, T = case["B"], case["T"]
     t = lambda x: torch.tensor(x, dtype=torch.float32, requires_grad=True)  # noqa: E731
+    if kind == "phase2":
+        res = {}
+        D = case["D"]
+        pv = torch.tensor(inp["partial_value"].reshape(B, T, D), requires_grad=True)
+        io = torch.tensor(inp["interblock_output"].reshape(B, T, D), requires_grad=True)
+        lse = torch.tensor(inp["interblock_lse"].reshape(B, T), requires_grad=True)
+        bias = torch.tensor(inp["logit_bias"], requires_grad=True) if case.get("bias") else 0.0
+        norm_out = case.get("normalize_output", False)
+        if case["mode"] == "lrid":
+            pk = torch.tensor(inp["partial_key"].reshape(B, T, -1), requires_grad=True)
+            q = torch.tensor(inp["query"], requires_grad=True)
+            out = ref.lrid_attention_residual_phase2(pv, pk, q, io, lse, case["scale"], case["key_norm"],
+                                                     normalize_output=norm_out, logit_bias=bias)
+        elif case["mode"] == "base":
+            q = torch.tensor(inp["query"], requires_grad=True)
+            out = ref.attention_residual_phase2(pv, q, io, lse, case["key_norm"], normalize_output=norm_out,
+                                                logit_bias=bias)
+        else:
+            lg = torch.tensor(inp["partial_logit"].reshape(B, T), requires_grad=True)
+            out = ref.attention_residual_phase2_from_logit(pv, lg, io, lse, normalize_output=norm_out)
+        out.backward(torch.tensor(inp["grad_output"].reshape(B, T, D)))
+        res["out"] = out.detach().numpy().reshape(B * T, D)
+        res["d_partial_value"] = pv.grad.numpy().reshape(B * T, D)
+        res["d_interblock_output"] = io.grad.numpy().reshape(B * T, D)
+        res["d_interblock_lse"] = lse.grad.numpy().reshape(B * T)
+        if case["mode"] == "lrid":
+            res["d_partial_key"] = pk.grad.numpy().reshape(B * T, -1)
+        if case["mode"] in ("lrid", "base"):
+            res["dq"] = q.grad.numpy().reshape(-1)
+        else:
+            res["d_partial_logit"] = lg.grad.numpy().reshape(B * T)
+        if case.get("bias"):
+            res["dbias"] = np.array(bias.grad.item(), dtype=np.float32)
+        return {k: np.asarray(v) for k, v in res.items()}
     values = [t(v.reshape(B, T, -1)) for v in inp["values"]]
     grad_out = (torch.tensor(inp["grad_output"].reshape(B, T, -1), dtype=torch.float32)
-                if kind != "phase1" else None)
+                if kind not in ("phase1", "phase2") else None)
     res = {}
     if kind == "phase1":
         Q = case["Q"]
@@ -140,7 +174,10 @@ def main():
     import torch
 
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    only = sys.argv[1:]  # optional case-name prefixes: regenerate just those
     for case in CASES:
+        if only and not any(case["name"].startswith(o) for o in only):
+            continue
         res = run_case(ref, case)
         path = os.path.join(HERE, case["name"] + ".npz")
         np.savez_compressed(path, **res)

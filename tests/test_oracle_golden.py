@@ -19,12 +19,14 @@ F32_EPS = float(np.finfo(np.float32).eps)
 def oracle_case(case):
     inp = case_inputs(case)
     norm = oracle.NORM_NONE
-    if case.get("normalize_output") and case["kind"] != "phase1":
+    if case.get("normalize_output") and case["kind"] not in ("phase1", "phase2"):
         if case["kind"] == "base":
             norm = oracle.NORM_ROW
         else:
             norm = oracle.NORM_PER_HEAD if case["H"] == 1 else oracle.NORM_ROW
     bias = inp["logit_bias"] if case.get("bias") else None
+    if case["kind"] == "phase2":
+        return oracle_phase2(case, inp)
     if case["kind"] == "phase1":
         nrm = case.get("normalize_output", False)
         out, lse, _, _, _ = oracle.phase1_forward(inp["values"], inp["logits"], nrm)
@@ -56,6 +58,27 @@ def oracle_case(case):
     return out, grads
 
 
+def phase2_args(case, inp):
+    """Keyword arguments of oracle.phase2_forward/backward for a phase-2 case,
+    with the reference's eps choices: fp32 eps for the LRID key norm
+    (_norm(partial_key.float())), the value dtype's eps (fp32 here) for the
+    base key norm and the output norm."""
+    mode = {"lrid": oracle.PHASE2_LRID, "base": oracle.PHASE2_BASE, "logit": oracle.PHASE2_LOGIT}[case["mode"]]
+    kw = dict(partial_key=inp.get("partial_key"), query=inp.get("query"), partial_logit=inp.get("partial_logit"),
+              logit_scale=case.get("scale", 1.0), key_norm=case.get("key_norm", False),
+              logit_bias=float(inp["logit_bias"]) if case.get("bias") else 0.0,
+              normalize_output=case.get("normalize_output", False))
+    return mode, kw
+
+
+def oracle_phase2(case, inp):
+    mode, kw = phase2_args(case, inp)
+    base = (inp["partial_value"], inp["interblock_output"], inp["interblock_lse"])
+    out, _ = oracle.phase2_forward(mode, *base, **kw)
+    grads = oracle.phase2_backward(mode, *base, inp["grad_output"], **kw)
+    return out, grads
+
+
 def _close(name, actual, expected, scale=1.0):
     expected = np.asarray(expected, np.float64)
     tol = 2e-5 * scale * max(1.0, float(np.abs(expected).max(initial=0.0)))
@@ -76,6 +99,9 @@ def test_oracle_matches_reference_golden(case):
                 _close(name + "_sum", got.sum(axis=(1, 2)), gold[name + "_sum"], scale=10.0)
                 got = got[:, :keep]
             _close(name, got, gold[name])
+    for name in ("d_partial_value", "d_interblock_output", "d_interblock_lse", "d_partial_key", "d_partial_logit"):
+        if name in gold:
+            _close(name, grads[name], gold[name])
     for name in ("lse", "dlogits"):
         if name in gold:
             _close(name, grads[name], gold[name])
@@ -83,7 +109,7 @@ def test_oracle_matches_reference_golden(case):
         _close("dW", grads["dW"], gold["dW"], scale=4.0)
     for name in ("dq", "dgate", "dq_dynamic", "dbias"):
         if name in gold:
-            _close(name, grads[name].reshape(gold[name].shape), gold[name], scale=4.0)
+            _close(name, np.asarray(grads[name]).reshape(gold[name].shape), gold[name], scale=4.0)
 
 
 def test_count_prior_zero_query_is_count_weighted_mean():
