@@ -265,6 +265,50 @@ int attnres_block_summary_backward(int64_t num_elements, int dtype, const void* 
                                    const void* sum, const float* scale_device, float scale, void* grad_partial,
                                    float* grad_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Phase-2 key modes: the partial block's logit from an LRID key, from the base
+ * key rms_norm(partial_value), or given. */
+enum { ATTNRES_PHASE2_LRID = 0, ATTNRES_PHASE2_BASE = 1, ATTNRES_PHASE2_LOGIT = 2 };
+
+/*
+ * Cached-logit phase 2: merge the live partial block into the phase-1 result.
+ *   logit = scale * <k_hat, query> + bias   (LRID: k = partial_key [N, key_dim],
+ *           scale = logit_scale; BASE: k = partial_value, scale 1; LOGIT: given
+ *           float partial_logit [N]); k_hat = rms-normalised k when key_norm
+ *   p = sigmoid(logit - interblock_lse[n]),  out = prev + p * (partial - prev)
+ * optionally rms-normalised per row (output_inv_rms float [N] then written).
+ * partial_value, interblock_output, output: dtype [N, value_dim] dense;
+ * query: dtype [key_dim] (LRID) or [value_dim] (BASE); bias = *logit_bias_device
+ * when not NULL, else logit_bias. Replaces lrid_attention_residual_phase2
+ * (attnres_ops.py:4075-4139), attention_residual_phase2 (:3964-4019) and
+ * attention_residual_phase2_from_logit (:4043-4072).
+ */
+int attnres_phase2_forward(int mode, int64_t num_tokens, int value_dim, int key_dim, int dtype,
+                           const void* partial_value, const void* partial_key, const float* partial_logit,
+                           const void* query, float logit_scale, int key_norm, float key_eps, float logit_bias,
+                           const float* logit_bias_device, const void* interblock_output,
+                           const float* interblock_lse, int normalize_output, float output_eps, void* output,
+                           float* output_inv_rms, void* stream);
+/*
+ * Phase-2 backward. grad_partial_value / grad_interblock_output: dtype [N, value_dim];
+ * grad_interblock_lse: float [N]; grad_partial_key (LRID): dtype [N, key_dim];
+ * grad_partial_logit (LOGIT): float [N]; grad_query (float [key_dim] or
+ * [value_dim]) and grad_bias (float, one element) may be NULL and are summed
+ * over tokens in a fixed order (deterministic) with a workspace of
+ * attnres_phase2_backward_workspace_bytes(...) bytes. With normalize_output the
+ * forward's output and output_inv_rms are passed back. Replaces the autograd
+ * backward of the same functions (Triton kernel attnres_ops.py:2058-2121).
+ */
+size_t attnres_phase2_backward_workspace_bytes(int mode, int64_t num_tokens, int value_dim, int key_dim);
+int attnres_phase2_backward(int mode, int64_t num_tokens, int value_dim, int key_dim, int dtype,
+                            const void* partial_value, const void* partial_key, const float* partial_logit,
+                            const void* query, float logit_scale, int key_norm, float key_eps, float logit_bias,
+                            const float* logit_bias_device, const void* interblock_output,
+                            const float* interblock_lse, int normalize_output, const void* output,
+                            const float* output_inv_rms, const void* grad_output, void* grad_partial_value,
+                            void* grad_partial_key, float* grad_partial_logit, void* grad_interblock_output,
+                            float* grad_interblock_lse, float* grad_query, float* grad_bias, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /*
  * Cached-logit block read ("phase 1"): Q reads of the same S sources whose
  * logits were computed once. Replaces attention_residual_phase1_from_logits

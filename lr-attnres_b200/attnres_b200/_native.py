@@ -40,6 +40,9 @@ EXPORTED_SYMBOLS = (
     "attnres_block_summary_forward",
     "attnres_block_summary_backward_workspace_bytes",
     "attnres_block_summary_backward",
+    "attnres_phase2_forward",
+    "attnres_phase2_backward_workspace_bytes",
+    "attnres_phase2_backward",
     "attnres_phase1_forward",
     "attnres_phase1_backward",
     "attnres_noalloc_scratch_bytes",
@@ -122,6 +125,24 @@ def load(path=None):
     L.attnres_block_summary_backward_workspace_bytes.argtypes = [I64]
     L.attnres_block_summary_backward.restype = I
     L.attnres_block_summary_backward.argtypes = [I64, I, P, P, P, P, F, P, P, P, SZ, P]
+    L.attnres_phase2_forward.restype = I
+    L.attnres_phase2_forward.argtypes = [
+        I, I64, I, I, I,             # mode, N, value_dim, key_dim, dtype
+        P, P, P, P,                  # partial value, partial key, partial logit, query
+        F, I, F, F, P,               # logit scale, key norm, key eps, bias, bias (device)
+        P, P, I, F, P, P, P,         # interblock output, lse, normalize, output eps, output, inv, stream
+    ]
+    L.attnres_phase2_backward_workspace_bytes.restype = SZ
+    L.attnres_phase2_backward_workspace_bytes.argtypes = [I, I64, I, I]
+    L.attnres_phase2_backward.restype = I
+    L.attnres_phase2_backward.argtypes = [
+        I, I64, I, I, I,             # mode, N, value_dim, key_dim, dtype
+        P, P, P, P,                  # partial value, partial key, partial logit, query
+        F, I, F, F, P,               # logit scale, key norm, key eps, bias, bias (device)
+        P, P, I, P, P, P,            # interblock output, lse, normalize, output, output inv, grad output
+        P, P, P, P, P, P, P,         # grads: partial value, key, logit, interblock output, lse, query, bias
+        P, SZ, P,                    # workspace, bytes, stream
+    ]
     L.attnres_phase1_forward.restype = I
     L.attnres_phase1_forward.argtypes = [I, I, I64, I, I, PP, PI64, P, I, I, F, P, P, P, P]
     L.attnres_phase1_backward.restype = I

@@ -1146,3 +1146,194 @@ def attention_residual_block_summary(partial_block: Optional[Tensor], layer_outp
         c = torch.exp(-alpha * alpha.new_tensor(float(count)).log())
         return block_summary(partial_block, layer_output, c.to(dtype), 1.0)
     return block_summary(partial_block, layer_output, None, float(count) ** (-float(alpha)))
+
+
+# ---------------------------------------------------------------------------
+# attnres::phase2 — cached-logit phase 2 (merge of the live partial block)
+# ---------------------------------------------------------------------------
+PHASE2_LRID, PHASE2_BASE, PHASE2_LOGIT = 0, 1, 2
+
+
+def _phase2_key_eps(mode, dtype):
+    # LRID keys are normed as _norm(partial_key.float()) (attnres_ops.py:4127);
+    # the base key as _norm(partial_value) in the value dtype (:2638)
+    return float(torch.finfo(torch.float32 if mode == PHASE2_LRID else dtype).eps)
+
+
+@torch.library.custom_op("attnres::phase2", mutates_args=())
+def phase2(mode: int, partial_value: Tensor, partial_key: Optional[Tensor], partial_logit: Optional[Tensor],
+           query: Optional[Tensor], interblock_output: Tensor, interblock_lse: Tensor, logit_scale: float,
+           key_norm: bool, logit_bias: Optional[Tensor], logit_bias_value: float,
+           normalize_output: bool) -> tuple[Tensor, Tensor]:
+    """Returns (output [*, d] value dtype, output inverse rms [N] fp32 or [1])."""
+    _require_cuda([partial_value, partial_key, partial_logit, query, interblock_output, interblock_lse, logit_bias],
+                  "phase-2 inputs")
+    dtype = partial_value.dtype
+    d = partial_value.size(-1)
+    n = _ntok(partial_value)
+    pv = partial_value.reshape(n, d).contiguous()
+    io = interblock_output.to(dtype).reshape(n, d).contiguous()
+    lse = interblock_lse.to(torch.float32).reshape(n).contiguous()
+    pk = None if partial_key is None else partial_key.to(dtype).reshape(n, -1).contiguous()
+    lg = None if partial_logit is None else partial_logit.to(torch.float32).reshape(n).contiguous()
+    q = None if query is None else query.reshape(-1).to(dtype).contiguous()
+    R = pk.size(1) if pk is not None else 0
+    b = None if logit_bias is None else logit_bias.to(torch.float32).reshape(1).contiguous()
+    out = torch.empty((n, d), device=pv.device, dtype=dtype)
+    inv = torch.empty((n,) if normalize_output else (1,), device=pv.device, dtype=torch.float32)
+    with torch.cuda.device(pv.device):
+        rc = N.load().attnres_phase2_forward(
+            int(mode), n, d, R, _dtype_code(dtype), _ptr(pv), _ptr(pk), _ptr(lg), _ptr(q), float(logit_scale),
+            int(bool(key_norm)), _phase2_key_eps(mode, dtype), float(logit_bias_value), _ptr(b), _ptr(io), _ptr(lse),
+            int(bool(normalize_output)), float(torch.finfo(dtype).eps), _ptr(out), _ptr(inv),
+            _stream_ptr(pv.device))
+    N.check(rc, "attnres_phase2_forward")
+    return out.reshape(partial_value.shape), inv
+
+
+@phase2.register_fake
+def _(mode, partial_value, partial_key, partial_logit, query, interblock_output, interblock_lse, logit_scale,
+      key_norm, logit_bias, logit_bias_value, normalize_output):
+    n = partial_value.numel() // partial_value.size(-1)
+    return partial_value.new_empty(partial_value.shape), partial_value.new_empty(
+        (n,) if normalize_output else (1,), dtype=torch.float32)
+
+
+@torch.library.custom_op("attnres::phase2_backward", mutates_args=())
+def phase2_backward(mode: int, partial_value: Tensor, partial_key: Optional[Tensor], partial_logit: Optional[Tensor],
+                    query: Optional[Tensor], interblock_output: Tensor, interblock_lse: Tensor, logit_scale: float,
+                    key_norm: bool, logit_bias: Optional[Tensor], logit_bias_value: float, normalize_output: bool,
+                    output: Tensor, output_inv_rms: Tensor, grad_output: Tensor, want_query_grad: bool,
+                    want_bias_grad: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (d partial_value, d partial_key, d partial_logit, d interblock_output,
+    d interblock_lse, d query, d bias); the unused ones are empty."""
+    dtype = partial_value.dtype
+    d = partial_value.size(-1)
+    n = _ntok(partial_value)
+    dev = partial_value.device
+    pv = partial_value.reshape(n, d).contiguous()
+    io = interblock_output.to(dtype).reshape(n, d).contiguous()
+    lse = interblock_lse.to(torch.float32).reshape(n).contiguous()
+    pk = None if partial_key is None else partial_key.to(dtype).reshape(n, -1).contiguous()
+    lg = None if partial_logit is None else partial_logit.to(torch.float32).reshape(n).contiguous()
+    q = None if query is None else query.reshape(-1).to(dtype).contiguous()
+    R = pk.size(1) if pk is not None else 0
+    b = None if logit_bias is None else logit_bias.to(torch.float32).reshape(1).contiguous()
+    g = grad_output.to(dtype).reshape(n, d).contiguous()
+    y = output.to(dtype).reshape(n, d).contiguous() if normalize_output else None
+    yi = output_inv_rms.contiguous() if normalize_output else None
+    e = lambda: torch.empty((0,), device=dev, dtype=torch.float32)  # noqa: E731  (distinct, non-aliased)
+    dpv = torch.empty((n, d), device=dev, dtype=dtype)
+    dio = torch.empty((n, d), device=dev, dtype=dtype)
+    dlse = torch.empty((n,), device=dev, dtype=torch.float32)
+    dpk = torch.empty((n, R), device=dev, dtype=dtype) if pk is not None else e()
+    dlg = torch.empty((n,), device=dev, dtype=torch.float32) if lg is not None else e()
+    qn = (R if mode == PHASE2_LRID else d)
+    dq = torch.empty((qn,), device=dev, dtype=torch.float32) if (want_query_grad and q is not None) else e()
+    db = torch.empty((1,), device=dev, dtype=torch.float32) if want_bias_grad else e()
+    L = N.load()
+    ws_bytes = L.attnres_phase2_backward_workspace_bytes(int(mode), n, d, R)
+    ws = torch.empty((max(ws_bytes, 1),), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        rc = L.attnres_phase2_backward(
+            int(mode), n, d, R, _dtype_code(dtype), _ptr(pv), _ptr(pk), _ptr(lg), _ptr(q), float(logit_scale),
+            int(bool(key_norm)), _phase2_key_eps(mode, dtype), float(logit_bias_value), _ptr(b), _ptr(io), _ptr(lse),
+            int(bool(normalize_output)), _ptr(y), _ptr(yi), _ptr(g), _ptr(dpv),
+            _ptr(dpk) if pk is not None else None, _ptr(dlg) if lg is not None else None, _ptr(dio), _ptr(dlse),
+            _ptr(dq) if dq.numel() else None, _ptr(db) if want_bias_grad else None, _ptr(ws), ws_bytes,
+            _stream_ptr(dev))
+    N.check(rc, "attnres_phase2_backward")
+    return dpv, dpk, dlg, dio, dlse, dq, db
+
+
+@phase2_backward.register_fake
+def _(mode, partial_value, partial_key, partial_logit, query, interblock_output, interblock_lse, logit_scale,
+      key_norm, logit_bias, logit_bias_value, normalize_output, output, output_inv_rms, grad_output,
+      want_query_grad, want_bias_grad):
+    n = partial_value.numel() // partial_value.size(-1)
+    d = partial_value.size(-1)
+    f = partial_value.new_empty
+    R = 0 if partial_key is None else partial_key.numel() // n
+    return (f((n, d)), f((n, R)) if partial_key is not None else f((0,), dtype=torch.float32),
+            f((n,), dtype=torch.float32) if partial_logit is not None else f((0,), dtype=torch.float32), f((n, d)),
+            f((n,), dtype=torch.float32),
+            f((R if mode == PHASE2_LRID else d,), dtype=torch.float32) if (want_query_grad and query is not None)
+            else f((0,), dtype=torch.float32),
+            f((1,), dtype=torch.float32) if want_bias_grad else f((0,), dtype=torch.float32))
+
+
+def _phase2_setup(ctx, inputs, output):
+    (mode, pv, pk, lg, q, io, lse, scale, key_norm, bias, bias_value, normalize_output) = inputs
+    out, inv = output
+    ctx.args = (int(mode), float(scale), bool(key_norm), float(bias_value), bool(normalize_output))
+    ctx.has = (pk is not None, lg is not None, q is not None, bias is not None)
+    ctx.meta = dict(pv=(pv.shape, pv.dtype), io=(io.shape, io.dtype), lse=(lse.shape, lse.dtype),
+                    pk=None if pk is None else (pk.shape, pk.dtype), lg=None if lg is None else (lg.shape, lg.dtype),
+                    q=None if q is None else (q.shape, q.dtype), b=None if bias is None else (bias.shape, bias.dtype))
+    opt = [t for t in (pk, lg, q, bias) if t is not None]
+    ctx.save_for_backward(pv, io, lse, out, inv, *opt)
+
+
+def _phase2_bwd(ctx, grad_out, grad_inv):
+    pv, io, lse, out, inv, *opt = ctx.saved_tensors
+    it = iter(opt)
+    pk, lg, q, bias = (next(it) if h else None for h in ctx.has)
+    mode, scale, key_norm, bias_value, normalize_output = ctx.args
+    want_q = q is not None and ctx.needs_input_grad[4]
+    want_b = bias is not None and ctx.needs_input_grad[9]
+    dpv, dpk, dlg, dio, dlse, dq, db = phase2_backward(mode, pv, pk, lg, q, io, lse, scale, key_norm, bias,
+                                                       bias_value, normalize_output, out, inv, grad_out, want_q,
+                                                       want_b)
+    m = ctx.meta
+
+    def cast(t, key):
+        shape, dtype = m[key]
+        return t.reshape(shape).to(dtype)
+
+    return (None, cast(dpv, "pv"), cast(dpk, "pk") if pk is not None else None,
+            cast(dlg, "lg") if lg is not None else None, cast(dq, "q") if want_q else None, cast(dio, "io"),
+            cast(dlse, "lse"), None, None, cast(db, "b") if want_b else None, None, None)
+
+
+phase2.register_autograd(_phase2_bwd, setup_context=_phase2_setup)
+
+
+def _phase2_bias(logit_bias):
+    """(tensor, value) for a logit bias given as None, a float or a tensor
+    (attnres_ops.py:108-120)."""
+    if logit_bias is None:
+        return None, 0.0
+    if isinstance(logit_bias, Tensor):
+        return logit_bias, 0.0
+    return None, float(logit_bias)
+
+
+def lrid_attention_residual_phase2(partial_value: Tensor, partial_key: Tensor, query: Tensor,
+                                   interblock_output: Tensor, interblock_lse: Tensor, logit_scale: float,
+                                   key_norm: bool, force_triton: bool = False, normalize_output: bool = False,
+                                   logit_bias=0.0) -> Tensor:
+    """attnres_ops.py:4075-4139 on the B200 kernel: merge of the live partial
+    block (LRID key, one query) into the phase-1 result."""
+    bt, bv = _phase2_bias(logit_bias)
+    out, _ = phase2(PHASE2_LRID, partial_value, partial_key, None, query, interblock_output, interblock_lse,
+                    float(logit_scale), bool(key_norm), bt, bv, bool(normalize_output))
+    return out
+
+
+def attention_residual_phase2(partial_value: Tensor, query: Tensor, interblock_output: Tensor,
+                              interblock_lse: Tensor, key_norm: bool, force_triton: bool = False,
+                              normalize_output: bool = False, logit_bias=0.0) -> Tensor:
+    """attnres_ops.py:3964-4019 on the B200 kernel: base key rms_norm(partial)."""
+    bt, bv = _phase2_bias(logit_bias)
+    out, _ = phase2(PHASE2_BASE, partial_value, None, None, query, interblock_output, interblock_lse, 1.0,
+                    bool(key_norm), bt, bv, bool(normalize_output))
+    return out
+
+
+def attention_residual_phase2_from_logit(partial_value: Tensor, partial_logit: Tensor, interblock_output: Tensor,
+                                         interblock_lse: Tensor, force_triton: bool = False,
+                                         normalize_output: bool = False) -> Tensor:
+    """attnres_ops.py:4043-4072 on the B200 kernel: the partial logit is given."""
+    out, _ = phase2(PHASE2_LOGIT, partial_value, None, partial_logit, None, interblock_output, interblock_lse, 1.0,
+                    False, None, 0.0, bool(normalize_output))
+    return out

@@ -554,6 +554,87 @@ int attnres_block_summary_backward(int64_t num_elements, int dtype, const void* 
   return ATTNRES_OK;
 }
 
+static int check_phase2(int mode, int64_t N, int d, int R, int dtype, const void* v, const void* key,
+                        const float* logit, const void* q, const void* prev, const float* lse) {
+  if (mode < ATTNRES_PHASE2_LRID || mode > ATTNRES_PHASE2_LOGIT)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown phase-2 mode %d", mode);
+  if (N < 0 || d < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2: num_tokens < 0 or value_dim < 1");
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (mode == ATTNRES_PHASE2_LRID && R < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2: key_dim < 1");
+  if (N == 0) return ATTNRES_OK;
+  if (!v || !prev || !lse) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2: NULL partial value / interblock");
+  if (mode == ATTNRES_PHASE2_LRID && (!key || !q)) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2: NULL key/query");
+  if (mode == ATTNRES_PHASE2_BASE && !q) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2: NULL query");
+  if (mode == ATTNRES_PHASE2_LOGIT && !logit) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2: NULL partial logit");
+  return ATTNRES_OK;
+}
+
+int attnres_phase2_forward(int mode, int64_t num_tokens, int value_dim, int key_dim, int dtype,
+                           const void* partial_value, const void* partial_key, const float* partial_logit,
+                           const void* query, float logit_scale, int key_norm, float key_eps, float logit_bias,
+                           const float* logit_bias_device, const void* interblock_output,
+                           const float* interblock_lse, int normalize_output, float output_eps, void* output,
+                           float* output_inv_rms, void* stream) {
+  int rc = check_phase2(mode, num_tokens, value_dim, key_dim, dtype, partial_value, partial_key, partial_logit, query,
+                        interblock_output, interblock_lse);
+  if (rc) return rc;
+  if (num_tokens == 0) return ATTNRES_OK;
+  if (!output || (normalize_output && !output_inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2: NULL output / output_inv_rms");
+  cudaError_t e = attnres::phase2_run(false, mode, num_tokens, value_dim, key_dim, dtype, partial_value, partial_key,
+                                      partial_logit, query, logit_scale, key_norm, key_eps, logit_bias,
+                                      logit_bias_device, interblock_output, interblock_lse, normalize_output,
+                                      output_eps, output, output_inv_rms, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                      nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_phase2_forward launch");
+  return ATTNRES_OK;
+}
+
+size_t attnres_phase2_backward_workspace_bytes(int mode, int64_t num_tokens, int value_dim, int key_dim) {
+  return attnres::phase2_workspace(mode, num_tokens, value_dim, key_dim);
+}
+
+int attnres_phase2_backward(int mode, int64_t num_tokens, int value_dim, int key_dim, int dtype,
+                            const void* partial_value, const void* partial_key, const float* partial_logit,
+                            const void* query, float logit_scale, int key_norm, float key_eps, float logit_bias,
+                            const float* logit_bias_device, const void* interblock_output,
+                            const float* interblock_lse, int normalize_output, const void* output,
+                            const float* output_inv_rms, const void* grad_output, void* grad_partial_value,
+                            void* grad_partial_key, float* grad_partial_logit, void* grad_interblock_output,
+                            float* grad_interblock_lse, float* grad_query, float* grad_bias, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  int rc = check_phase2(mode, num_tokens, value_dim, key_dim, dtype, partial_value, partial_key, partial_logit, query,
+                        interblock_output, interblock_lse);
+  if (rc) return rc;
+  if (num_tokens == 0) {
+    if (grad_query) cudaMemsetAsync(grad_query, 0, sizeof(float) * (mode == ATTNRES_PHASE2_LRID ? key_dim : value_dim),
+                                    static_cast<cudaStream_t>(stream));
+    if (grad_bias) cudaMemsetAsync(grad_bias, 0, sizeof(float), static_cast<cudaStream_t>(stream));
+    return ATTNRES_OK;
+  }
+  if (!grad_output || !grad_partial_value || !grad_interblock_output || !grad_interblock_lse)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2 backward: NULL gradient buffer");
+  if (mode == ATTNRES_PHASE2_LRID && !grad_partial_key)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2 backward: NULL grad_partial_key");
+  if (mode == ATTNRES_PHASE2_LOGIT && !grad_partial_logit)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2 backward: NULL grad_partial_logit");
+  if (normalize_output && (!output || !output_inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2 backward: the normalised output and its inverse rms are needed");
+  const bool need_ws = (grad_query && mode != ATTNRES_PHASE2_LOGIT) || grad_bias;
+  if (need_ws && (!workspace || workspace_bytes < attnres::phase2_workspace(mode, num_tokens, value_dim, key_dim)))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "phase 2 backward: workspace too small");
+  cudaError_t e = attnres::phase2_run(true, mode, num_tokens, value_dim, key_dim, dtype, partial_value, partial_key,
+                                      partial_logit, query, logit_scale, key_norm, key_eps, logit_bias,
+                                      logit_bias_device, interblock_output, interblock_lse, normalize_output, 0.f,
+                                      nullptr, nullptr, grad_output, output, output_inv_rms, grad_partial_value,
+                                      grad_partial_key, grad_partial_logit, grad_interblock_output,
+                                      grad_interblock_lse, grad_query, grad_bias, workspace,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_phase2_backward launch");
+  return ATTNRES_OK;
+}
+
 int attnres_phase1_forward(int num_sources, int num_queries, int64_t num_tokens, int value_dim, int dtype,
                            const void* const* values, const int64_t* value_row_strides, const void* logits,
                            int logit_dtype, int output_norm, float output_eps, void* output, float* lse,

@@ -168,6 +168,15 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
                                   float* grad_weight, void* workspace, size_t workspace_bytes, cudaStream_t st);
 cudaError_t read_keyproj_bwd_status(unsigned* status, bool reset);
 
+// Cached-logit phase 2 (phase2.cu).
+size_t phase2_workspace(int mode, long long N, int d, int R);
+cudaError_t phase2_run(bool bwd, int mode, long long N, int d, int R, int dtype, const void* v, const void* key,
+                       const float* logit, const void* q, float scale, int key_norm, float key_eps, float bias,
+                       const float* bias_dev, const void* prev, const float* lse, int onorm, float out_eps,
+                       void* out, float* out_inv, const void* g, const void* y, const float* y_inv, void* dv,
+                       void* dkey, float* dlogit, void* dprev, float* dlse, float* grad_query, float* grad_bias,
+                       void* workspace, cudaStream_t st);
+
 // Block summary (summary.cu).
 int summary_bwd_grid(long long n);
 cudaError_t summary_forward_launch(long long n, int dtype, const void* partial, const void* x,

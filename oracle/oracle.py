@@ -262,9 +262,12 @@ def phase2_forward(mode, partial_value, interblock_output, interblock_lse, parti
 def phase2_backward(mode, partial_value, interblock_output, interblock_lse, grad_output, partial_key=None,
                     query=None, partial_logit=None, logit_scale=1.0, key_norm=False,
                     key_eps=float(np.finfo(np.float32).eps), logit_bias=0.0, normalize_output=False,
-                    output_eps=float(np.finfo(np.float32).eps)):
+                    output_eps=float(np.finfo(np.float32).eps), saved_output=None):
     """Analytic gradients of phase2_forward (the reference's backward kernel
-    attnres_ops.py:2058-2121 and the autograd of its PyTorch path)."""
+    attnres_ops.py:2058-2121 and the autograd of its PyTorch path). With
+    normalize_output the output-norm backward uses `saved_output` when given:
+    the reference's backward kernel loads the saved, value-dtype output
+    (attnres_ops.py:2090-2093)."""
     v = np.asarray(partial_value, np.float64)
     prev = np.asarray(interblock_output, np.float64)
     out, st = phase2_forward(mode, partial_value, interblock_output, interblock_lse, partial_key, query,
@@ -272,7 +275,7 @@ def phase2_backward(mode, partial_value, interblock_output, interblock_lse, grad
                              output_eps)
     g = np.asarray(grad_output, np.float64)
     if normalize_output:
-        y = out
+        y = out if saved_output is None else np.asarray(saved_output, np.float64)
         g = st["inv"][:, None] * (g - y * (g * y).mean(-1, keepdims=True))
     p = st["p"]
     dl = p * (1.0 - p) * (g * (v - prev)).sum(-1)

@@ -37,5 +37,11 @@ def test_fake_shapes_of_all_ops():
         assert bo.shape == (B, T, D) and binv.shape == (B * T,)
         ssum, ssrc = ops.block_summary(v[0], v[1], None, 0.5)
         assert ssum.shape == (B, T, D) and ssrc.shape == (B, T, D)
+        p2o, p2i = ops.phase2(0, v[0], k[0], None, _fake(mode, R), v[1], _fake(mode, B, T, dtype=torch.float32),
+                              0.5, True, None, 0.0, True)
+        assert p2o.shape == (B, T, D) and p2i.shape == (B * T,)
+        p2g = ops.phase2_backward(0, v[0], k[0], None, _fake(mode, R), v[1], _fake(mode, B, T, dtype=torch.float32),
+                                  0.5, True, None, 0.0, True, p2o, p2i, g, True, False)
+        assert p2g[0].shape == (B * T, D) and p2g[1].shape == (B * T, R) and p2g[5].shape == (R,)
         gp, gsc = ops.block_summary_backward(g, None, ssum, _fake(mode, 1, dtype=torch.float32), 1.0, True)
         assert gp.shape == (B, T, D) and gsc.shape == (1,)
