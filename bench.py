@@ -458,7 +458,52 @@ def main():
         aux = {"block_summary": {"kernel": "summary_fwd_kernel (a9: sum = partial + x, source = sum * c)",
                                  "elements": xs.numel(), "ms": sms, "achieved_gbs": sbytes / sms / 1e6,
                                  "frac": sbytes / sms / 1e6 / hbm, "bytes": sbytes}}
-        del xs, ps
+        # cached-logit phase 2 (LRID key, one query) on the same 4x rows: forward
+        # and backward, each timed alone
+        R = c["R"]
+        pk = torch.randn(xs.shape[0], xs.shape[1], R, device=device, dtype=torch.bfloat16)
+        q2 = torch.randn(R, device=device, dtype=torch.bfloat16) * 0.1
+        lse2 = torch.randn(xs.shape[0], xs.shape[1], device=device)
+        p2 = torch.ops.attnres.phase2
+        p2b = torch.ops.attnres.phase2_backward
+
+        def p2f():
+            return p2(0, ps, pk, None, q2, xs, lse2, c["scale"], True, None, 0.0, False)
+
+        def p2g(o):
+            return p2b(0, ps, pk, None, q2, xs, lse2, c["scale"], True, None, 0.0, False, o[0], o[1], ps, True,
+                       False)
+
+        with torch.cuda.stream(stream):
+            o2 = p2f()
+            p2g(o2)
+        torch.cuda.synchronize()
+        gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gf, stream=stream):
+            o2 = p2f()
+        with torch.cuda.graph(gb, stream=stream):
+            p2g(o2)
+        ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                gf.replay()
+                gb.replay()
+            ev2[0].record(stream)
+            for _ in range(10):
+                gf.replay()
+            ev2[1].record(stream)
+            for _ in range(10):
+                gb.replay()
+            ev2[2].record(stream)
+        torch.cuda.synchronize()
+        fms, bms = ev2[0].elapsed_time(ev2[1]) / 10, ev2[1].elapsed_time(ev2[2]) / 10
+        ntok = xs.shape[0] * xs.shape[1]
+        fb = ntok * (3 * c["D"] + R) * 2 + ntok * 4
+        bb = ntok * (5 * c["D"] + 2 * R) * 2 + ntok * 8
+        aux["phase2"] = {"kernel": "phase2_fwd_kernel / phase2_bwd_kernel (LRID key, key norm)", "tokens": ntok,
+                         "fwd_ms": fms, "fwd_frac": fb / fms / 1e6 / hbm, "bwd_ms": bms,
+                         "bwd_frac": bb / bms / 1e6 / hbm, "fwd_bytes": fb, "bwd_bytes": bb}
+        del xs, ps, pk, o2
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not kv:
