@@ -85,11 +85,16 @@ class ClockSampler:
         self.proc = None
 
     def start(self):
+        """Starts nvidia-smi and waits for its first sample, so that sampling
+        covers the whole timed region that follows (nvidia-smi can take a
+        fraction of a second to start)."""
+        self.first = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.first = self.proc.stdout.readline()
         except Exception:
             self.proc = None
 
@@ -104,7 +109,10 @@ class ClockSampler:
             return None
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        lines = out.strip().splitlines()
+        if not lines and self.first:
+            lines = [self.first]  # a region shorter than one sampling period
+        for line in lines:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
                 continue

@@ -147,6 +147,85 @@ __device__ __forceinline__ float dot_pack(float acc, const float (&g)[VEC], cons
   return a0 + a1;
 }
 
+// ---------------------------------------------------------------------------
+// sm_100 mixed-precision FMA: fp32 accumulator += 16-bit a * 16-bit b, the
+// operands widened inside the FMA (no separate conversion instructions). The
+// 16-bit halves of a 32-bit word are taken as register halves.
+// ---------------------------------------------------------------------------
+template <typename T> struct Mixed16;
+template <> struct Mixed16<__nv_bfloat16> {
+  // a0 += lo(x) * w, a1 += hi(x) * w
+  static __device__ __forceinline__ void fma_w(float& a0, float& a1, uint32_t x, uint16_t w) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, l, %3, %0;\n\tfma.rn.f32.bf16 %1, h, %3, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(x), "h"(w));
+  }
+  // a0 += lo(x) * lo(y), a1 += hi(x) * hi(y)
+  static __device__ __forceinline__ void fma_pp(float& a0, float& a1, uint32_t x, uint32_t y) {
+    asm("{\n\t.reg .b16 xl, xh, yl, yh;\n\tmov.b32 {xl, xh}, %2;\n\tmov.b32 {yl, yh}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, xl, yl, %0;\n\tfma.rn.f32.bf16 %1, xh, yh, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(x), "r"(y));
+  }
+  // one chain each, element order lo then hi: ss += k*k, dot += k*q
+  static __device__ __forceinline__ void key_step(float& ss, float& dot, uint32_t k, uint32_t q) {
+    asm("{\n\t.reg .b16 kl, kh, ql, qh;\n\tmov.b32 {kl, kh}, %2;\n\tmov.b32 {ql, qh}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, kl, kl, %0;\n\tfma.rn.f32.bf16 %1, kl, ql, %1;\n\t"
+        "fma.rn.f32.bf16 %0, kh, kh, %0;\n\tfma.rn.f32.bf16 %1, kh, qh, %1;\n\t}"
+        : "+f"(ss), "+f"(dot)
+        : "r"(k), "r"(q));
+  }
+  static __device__ __forceinline__ uint16_t bits(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+  }
+};
+template <> struct Mixed16<__half> {
+  static __device__ __forceinline__ void fma_w(float& a0, float& a1, uint32_t x, uint16_t w) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "fma.rn.f32.f16 %0, l, %3, %0;\n\tfma.rn.f32.f16 %1, h, %3, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(x), "h"(w));
+  }
+  static __device__ __forceinline__ void fma_pp(float& a0, float& a1, uint32_t x, uint32_t y) {
+    asm("{\n\t.reg .b16 xl, xh, yl, yh;\n\tmov.b32 {xl, xh}, %2;\n\tmov.b32 {yl, yh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, xl, yl, %0;\n\tfma.rn.f32.f16 %1, xh, yh, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(x), "r"(y));
+  }
+  // one chain each, element order lo then hi: ss += k*k, dot += k*q
+  static __device__ __forceinline__ void key_step(float& ss, float& dot, uint32_t k, uint32_t q) {
+    asm("{\n\t.reg .b16 kl, kh, ql, qh;\n\tmov.b32 {kl, kh}, %2;\n\tmov.b32 {ql, qh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, kl, kl, %0;\n\tfma.rn.f32.f16 %1, kl, ql, %1;\n\t"
+        "fma.rn.f32.f16 %0, kh, kh, %0;\n\tfma.rn.f32.f16 %1, kh, qh, %1;\n\t}"
+        : "+f"(ss), "+f"(dot)
+        : "r"(k), "r"(q));
+  }
+  static __device__ __forceinline__ uint16_t bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
+};
+
+template <typename T> constexpr bool kIs16 = std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value;
+
+// acc[e] += w16 * x[e] over one pack (16-bit T; w16 = the weight in T's bits)
+template <typename T, int VEC>
+__device__ __forceinline__ void axpy_pack16(float (&acc)[VEC], uint16_t w16, const Pack<T, VEC>& x) {
+  const uint32_t* u = reinterpret_cast<const uint32_t*>(x.e);
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) Mixed16<T>::fma_w(acc[2 * i], acc[2 * i + 1], u[i], w16);
+}
+
+// acc + sum_e x[e] * y[e] over two packs (16-bit T), even and odd elements in
+// two chains like dot_pack (identical rounding: the widening is exact)
+template <typename T, int VEC>
+__device__ __forceinline__ float dot_pack16(float acc, const Pack<T, VEC>& x, const Pack<T, VEC>& y) {
+  const uint32_t* ux = reinterpret_cast<const uint32_t*>(x.e);
+  const uint32_t* uy = reinterpret_cast<const uint32_t*>(y.e);
+  float a0 = acc, a1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) Mixed16<T>::fma_pp(a0, a1, uy[i], ux[i]);
+  return a0 + a1;
+}
+
 template <typename T>
 __device__ __forceinline__ float load_f(const T* p) {
   return Elem<T>::to_f(__ldg(p));

@@ -210,6 +210,18 @@ __global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources 
   float q[KE];
 #pragma unroll
   for (int e = 0; e < KE; ++e) q[e] = qs[e];
+  // 16-bit T: the query also as packed pairs of T for the mixed-precision key
+  // dot products (the reference casts the query to the key dtype)
+  uint32_t q16[KE / 2];
+  auto pack_q16 = [&]() {
+    if constexpr (kIs16<T>) {
+#pragma unroll
+      for (int i = 0; i < KE / 2; ++i)
+        q16[i] = static_cast<uint32_t>(Mixed16<T>::bits(q[2 * i])) |
+                 (static_cast<uint32_t>(Mixed16<T>::bits(q[2 * i + 1])) << 16);
+    }
+  };
+  pack_q16();
 
   // Copy issue runs NSW - 1 units ahead of the consumer. Reaching a new token,
   // it records the token in the stage's slot; a token >= N ends the issue.
@@ -273,6 +285,7 @@ __global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources 
             q[pk * VEC + e] = (a.qmode == ATTNRES_QUERY_DYNAMIC) ? qd : qs[pk * VEC + e] + gate_k * qd;
           }
         }
+        pack_q16();
       }
       for (int r = 0; r < rounds; ++r) {
         const int seg = r * G + gidx;  // seg = s * H + h, h == kh
@@ -282,11 +295,17 @@ __global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources 
 #pragma unroll
           for (int pk = 0; pk < KP; ++pk) {
             const Pack<T, VEC> kr = lds_pack<T, VEC>(kt + s * R + kcol + pk * VEC);
+            if constexpr (kIs16<T>) {
+              const uint32_t* kw = reinterpret_cast<const uint32_t*>(kr.e);
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) {
-              const float x = Elem<T>::to_f(kr.e[e]);
-              ss = fmaf(x, x, ss);
-              dot = fmaf(x, q[pk * VEC + e], dot);
+              for (int i = 0; i < VEC / 2; ++i) Mixed16<T>::key_step(ss, dot, kw[i], q16[pk * VEC / 2 + i]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) {
+                const float x = Elem<T>::to_f(kr.e[e]);
+                ss = fmaf(x, x, ss);
+                dot = fmaf(x, q[pk * VEC + e], dot);
+              }
             }
           }
         }
@@ -345,10 +364,19 @@ __global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources 
         Pack<T, VEC> r4[4];
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) r4[jj] = lds_pack<T, VEC>(vt + (s0 + jj) * CW);
-        axpy_pack<T, VEC>(acc, w4.x, r4[0]);
-        axpy_pack<T, VEC>(acc, w4.y, r4[1]);
-        axpy_pack<T, VEC>(acc, w4.z, r4[2]);
-        axpy_pack<T, VEC>(acc, w4.w, r4[3]);
+        if constexpr (kIs16<T>) {
+          // weights rounded to T (as the reference's PyTorch path casts them),
+          // widened inside the FMA with the values: no conversion instructions
+          axpy_pack16<T, VEC>(acc, Mixed16<T>::bits(w4.x), r4[0]);
+          axpy_pack16<T, VEC>(acc, Mixed16<T>::bits(w4.y), r4[1]);
+          axpy_pack16<T, VEC>(acc, Mixed16<T>::bits(w4.z), r4[2]);
+          axpy_pack16<T, VEC>(acc, Mixed16<T>::bits(w4.w), r4[3]);
+        } else {
+          axpy_pack<T, VEC>(acc, w4.x, r4[0]);
+          axpy_pack<T, VEC>(acc, w4.y, r4[1]);
+          axpy_pack<T, VEC>(acc, w4.z, r4[2]);
+          axpy_pack<T, VEC>(acc, w4.w, r4[3]);
+        }
       }
       if (s0 < S) {
         const float4 w4 = *reinterpret_cast<const float4*>(al + s0);
@@ -359,7 +387,10 @@ __global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources 
           if (s0 + jj < S) r4[jj] = lds_pack<T, VEC>(vt + (s0 + jj) * CW);
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj)
-          if (s0 + jj < S) axpy_pack<T, VEC>(acc, wj[jj], r4[jj]);
+          if (s0 + jj < S) {
+            if constexpr (kIs16<T>) axpy_pack16<T, VEC>(acc, Mixed16<T>::bits(wj[jj]), r4[jj]);
+            else axpy_pack<T, VEC>(acc, wj[jj], r4[jj]);
+          }
       }
       store_pack<T, VEC>(static_cast<T*>(a.out) + t * d + col, acc);
       if (++hcnt == cph) {
@@ -368,11 +399,9 @@ __global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources 
       }
     } else {
       float gp[VEC];
-      {
-        const Pack<T, VEC> gr = lds_pack<T, VEC>(reinterpret_cast<const T*>(st) + S * CW + lane * VEC);
+      const Pack<T, VEC> gr = lds_pack<T, VEC>(reinterpret_cast<const T*>(st) + S * CW + lane * VEC);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) gp[e] = Elem<T>::to_f(gr.e[e]);
-      }
+      for (int e = 0; e < VEC; ++e) gp[e] = Elem<T>::to_f(gr.e[e]);
 #pragma unroll
       for (int s0 = 0; s0 < SMAX; s0 += 4) {
         if (s0 < S) {
@@ -384,7 +413,8 @@ __global__ void __launch_bounds__(BWD ? (SMAX > 16 ? kStreamBwdWarpsManySources 
           for (int jj = 0; jj < 4; ++jj) {
             if (s0 + jj < S) {
               const float wgt = al[s0 + jj];
-              dwp[s0 + jj] = dot_pack<T, VEC>(dwp[s0 + jj], gp, r4[jj]);
+              if constexpr (kIs16<T>) dwp[s0 + jj] = dot_pack16<T, VEC>(dwp[s0 + jj], r4[jj], gr);
+              else dwp[s0 + jj] = dot_pack<T, VEC>(dwp[s0 + jj], gp, r4[jj]);
               if (sgv[s0 + jj]) {
                 float gv[VEC];
 #pragma unroll
