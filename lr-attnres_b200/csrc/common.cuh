@@ -176,6 +176,13 @@ template <> struct Mixed16<__nv_bfloat16> {
         : "+f"(ss), "+f"(dot)
         : "r"(k), "r"(q));
   }
+  // one chain, element order lo then hi: ss += k*k
+  static __device__ __forceinline__ void sq_step(float& ss, uint32_t k) {
+    asm("{\n\t.reg .b16 kl, kh;\n\tmov.b32 {kl, kh}, %1;\n\t"
+        "fma.rn.f32.bf16 %0, kl, kl, %0;\n\tfma.rn.f32.bf16 %0, kh, kh, %0;\n\t}"
+        : "+f"(ss)
+        : "r"(k));
+  }
   static __device__ __forceinline__ uint16_t bits(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
   }
@@ -200,6 +207,13 @@ template <> struct Mixed16<__half> {
         "fma.rn.f32.f16 %0, kh, kh, %0;\n\tfma.rn.f32.f16 %1, kh, qh, %1;\n\t}"
         : "+f"(ss), "+f"(dot)
         : "r"(k), "r"(q));
+  }
+  // one chain, element order lo then hi: ss += k*k
+  static __device__ __forceinline__ void sq_step(float& ss, uint32_t k) {
+    asm("{\n\t.reg .b16 kl, kh;\n\tmov.b32 {kl, kh}, %1;\n\t"
+        "fma.rn.f32.f16 %0, kl, kl, %0;\n\tfma.rn.f32.f16 %0, kh, kh, %0;\n\t}"
+        : "+f"(ss)
+        : "r"(k));
   }
   static __device__ __forceinline__ uint16_t bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
 };

@@ -179,11 +179,9 @@ __global__ void __launch_bounds__(192, 1) keyproj_tc_kernel(const __grid_constan
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const Pack<T, 8> p = *reinterpret_cast<const Pack<T, 8>*>(rowp + ((c ^ (row & 7)) * 16));
+            const uint32_t* pw = reinterpret_cast<const uint32_t*>(p.e);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float x = Elem<T>::to_f(p.e[e]);
-              ss = fmaf(x, x, ss);
-            }
+            for (int e = 0; e < 4; ++e) Mixed16<T>::sq_step(ss, pw[e]);  // widened inside the FMA
           }
         }
         __syncwarp();
