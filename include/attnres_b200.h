@@ -265,6 +265,22 @@ int attnres_block_summary_backward(int64_t num_elements, int dtype, const void* 
                                    const void* sum, const float* scale_device, float scale, void* grad_partial,
                                    float* grad_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Per-head RMS norm of key rows: y[r, h*dk + j] = x[r, h*dk + j] * inv_rms[r, h],
+ * inv_rms = rsqrt(mean_j x^2 + eps), dk = width / num_heads, fp32 math, y and
+ * grad dense [rows, width]; x may be a strided slice (x_row_stride elements),
+ * e.g. the key columns of a projection output. inv_rms float [rows, num_heads]
+ * (may be NULL in the forward). Backward: grad_x = inv * (grad_y - y <grad_y, y> / dk)
+ * with y = x * inv recomputed in fp32 from the pre-norm rows x (row stride
+ * x_row_stride), written with row stride grad_x_row_stride. Replaces _norm_lrid_key
+ * (model.py:33-36) as LRIDFusedProjection.forward applies it (model.py:375-379).
+ */
+int attnres_head_rms_norm_forward(int64_t rows, int width, int num_heads, int dtype, const void* x,
+                                  int64_t x_row_stride, float eps, void* y, float* inv_rms, void* stream);
+int attnres_head_rms_norm_backward(int64_t rows, int width, int num_heads, int dtype, const void* grad_y,
+                                   const void* x, int64_t x_row_stride, const float* inv_rms, void* grad_x,
+                                   int64_t grad_x_row_stride, void* stream);
+
 /* Phase-2 key modes: the partial block's logit from an LRID key, from the base
  * key rms_norm(partial_value), or given. */
 enum { ATTNRES_PHASE2_LRID = 0, ATTNRES_PHASE2_BASE = 1, ATTNRES_PHASE2_LOGIT = 2 };

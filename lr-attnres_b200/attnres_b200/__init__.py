@@ -16,6 +16,7 @@ from .ops import (
     lrid_attention_residual_read,
     lrid_attention_residual_read_gated,
     lrid_attention_residual_read_key_from_value,
+    lrid_fused_projection_forward,
     lrid_kv_read,
     lrid_read,
     lrid_read_list,
@@ -32,6 +33,7 @@ __all__ = [
     "lrid_attention_residual_read",
     "lrid_attention_residual_read_gated",
     "lrid_attention_residual_read_key_from_value",
+    "lrid_fused_projection_forward",
     "lrid_kv_read",
     "lrid_read",
     "lrid_read_list",

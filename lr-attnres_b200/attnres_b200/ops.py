@@ -1337,3 +1337,120 @@ def attention_residual_phase2_from_logit(partial_value: Tensor, partial_logit: T
     out, _ = phase2(PHASE2_LOGIT, partial_value, None, partial_logit, None, interblock_output, interblock_lse, 1.0,
                     False, None, 0.0, bool(normalize_output))
     return out
+
+
+# ---------------------------------------------------------------------------
+# attnres::lrid_fused_projection — LRIDFusedProjection.forward (model.py:363-388)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("attnres::lrid_fused_projection", mutates_args=())
+def lrid_fused_projection(x: Tensor, weight: Tensor, output_dim: int, rank: int, num_heads: int, key_norm: bool,
+                          query_rank: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """The projection x @ weight^T with weight [output_dim + rank + query_rank, in],
+    returned as (output [*, output_dim] contiguous, key [*, rank] (per-head rms
+    normalised when key_norm), query [*, query_rank] or empty, key inverse rms
+    [N, num_heads] fp32 or empty). The output and the key/query columns come
+    from two library GEMMs straight into their own buffers (the reference's
+    single GEMM is followed by a .contiguous() copy of the output columns); the
+    key norm reads the key columns in place."""
+    _require_cuda([x, weight], "fused projection inputs")
+    dt = x.dtype
+    n = x.numel() // x.size(-1)
+    x2 = x.reshape(n, x.size(-1))
+    w = weight.to(dt)
+    lead = x.shape[:-1]
+    out = torch.matmul(x2, w[:output_dim].t())
+    kq = torch.matmul(x2, w[output_dim:output_dim + rank + query_rank].t())  # [n, rank + query_rank]
+    e = lambda: x.new_empty((0,), dtype=torch.float32)  # noqa: E731
+    if key_norm:
+        key = torch.empty((n, rank), device=x.device, dtype=dt)
+        inv = torch.empty((n, num_heads), device=x.device, dtype=torch.float32)
+        with torch.cuda.device(x.device):
+            rc = N.load().attnres_head_rms_norm_forward(n, rank, num_heads, _dtype_code(dt), _ptr(kq), kq.stride(0),
+                                                         float(torch.finfo(dt).eps), _ptr(key), _ptr(inv),
+                                                         _stream_ptr(x.device))
+        N.check(rc, "attnres_head_rms_norm_forward")
+    else:
+        key = kq[:, :rank].contiguous()
+        inv = e()
+    query = kq[:, rank:].contiguous() if query_rank else x.new_empty((0,))
+    return (out.reshape(*lead, output_dim), key.reshape(*lead, rank),
+            query.reshape(*lead, query_rank) if query_rank else query, inv)
+
+
+@lrid_fused_projection.register_fake
+def _(x, weight, output_dim, rank, num_heads, key_norm, query_rank):
+    lead = x.shape[:-1]
+    n = x.numel() // x.size(-1)
+    return (x.new_empty((*lead, output_dim)), x.new_empty((*lead, rank)),
+            x.new_empty((*lead, query_rank)) if query_rank else x.new_empty((0,)),
+            x.new_empty((n, num_heads) if key_norm else (0,), dtype=torch.float32))
+
+
+@torch.library.custom_op("attnres::lrid_fused_projection_backward", mutates_args=())
+def lrid_fused_projection_backward(x: Tensor, weight: Tensor, key: Tensor, key_inv: Tensor,
+                                   grad_output: Optional[Tensor], grad_key: Optional[Tensor],
+                                   grad_query: Optional[Tensor], output_dim: int, rank: int, num_heads: int,
+                                   key_norm: bool, query_rank: int) -> tuple[Tensor, Tensor]:
+    """(d x, d weight [output_dim + rank + query_rank, in] in weight's dtype)."""
+    dt = x.dtype
+    n = x.numel() // x.size(-1)
+    x2 = x.reshape(n, x.size(-1))
+    w = weight.to(dt)
+    ncols = output_dim + rank + query_rank
+    # gradient of the projected columns [n, output_dim + rank + query_rank]
+    gp = torch.zeros((n, ncols), device=x.device, dtype=dt)
+    if grad_output is not None:
+        gp[:, :output_dim] = grad_output.reshape(n, output_dim)
+    if grad_key is not None:
+        gk = grad_key.to(dt).reshape(n, rank).contiguous()
+        if key_norm:
+            # the pre-norm key columns, re-projected (an [n, rank] GEMM), so the
+            # norm backward works from them in fp32 as torch's rms_norm does
+            kraw = torch.matmul(x2, w[output_dim:output_dim + rank].t())
+            kview = gp[:, output_dim:output_dim + rank]
+            with torch.cuda.device(x.device):
+                rc = N.load().attnres_head_rms_norm_backward(n, rank, num_heads, _dtype_code(dt), _ptr(gk),
+                                                             _ptr(kraw), kraw.stride(0), _ptr(key_inv), _ptr(kview),
+                                                             gp.stride(0), _stream_ptr(x.device))
+            N.check(rc, "attnres_head_rms_norm_backward")
+        else:
+            gp[:, output_dim:output_dim + rank] = gk
+    if grad_query is not None and query_rank:
+        gp[:, output_dim + rank:] = grad_query.reshape(n, query_rank)
+    dx = torch.matmul(gp, w[:ncols]).reshape(x.shape)
+    dw = torch.zeros_like(weight)
+    dw[:ncols] = torch.matmul(gp.t(), x2).to(weight.dtype)
+    return dx, dw
+
+
+@lrid_fused_projection_backward.register_fake
+def _(x, weight, key, key_inv, grad_output, grad_key, grad_query, output_dim, rank, num_heads, key_norm, query_rank):
+    return x.new_empty(x.shape), weight.new_empty(weight.shape)
+
+
+def _lfp_setup(ctx, inputs, output):
+    x, weight, output_dim, rank, num_heads, key_norm, query_rank = inputs
+    out, key, query, inv = output
+    ctx.args = (int(output_dim), int(rank), int(num_heads), bool(key_norm), int(query_rank))
+    ctx.save_for_backward(x, weight, key, inv)
+
+
+def _lfp_bwd(ctx, g_out, g_key, g_query, g_inv):
+    x, weight, key, inv = ctx.saved_tensors
+    output_dim, rank, num_heads, key_norm, query_rank = ctx.args
+    dx, dw = lrid_fused_projection_backward(x, weight, key, inv, g_out, g_key, g_query if query_rank else None,
+                                            output_dim, rank, num_heads, key_norm, query_rank)
+    return dx, dw, None, None, None, None, None
+
+
+lrid_fused_projection.register_autograd(_lfp_bwd, setup_context=_lfp_setup)
+
+
+def lrid_fused_projection_forward(x: Tensor, weight: Tensor, output_dim: int, rank: int, num_heads: int,
+                                  key_norm: bool, query_rank: int = 0):
+    """LRIDFusedProjection.forward (model.py:363-388) for the fused-key layout
+    (use_key, optionally use_fused_query): returns (output, key) or
+    (output, key, query) like the reference module."""
+    out, key, query, _ = lrid_fused_projection(x, weight, int(output_dim), int(rank), int(num_heads),
+                                               bool(key_norm), int(query_rank))
+    return (out, key, query) if query_rank else (out, key)

@@ -635,6 +635,36 @@ int attnres_phase2_backward(int mode, int64_t num_tokens, int value_dim, int key
   return ATTNRES_OK;
 }
 
+int attnres_head_rms_norm_forward(int64_t rows, int width, int num_heads, int dtype, const void* x,
+                                  int64_t x_row_stride, float eps, void* y, float* inv_rms, void* stream) {
+  if (rows < 0 || width < 1 || num_heads < 1 || width % num_heads)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "head rms norm: width must divide by num_heads");
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (x_row_stride < width) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "head rms norm: x_row_stride < width");
+  if (rows > 0 && (!x || !y)) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "head rms norm: NULL x/y");
+  cudaError_t e = attnres::headnorm_launch(false, dtype, rows, width, num_heads, x, x_row_stride, eps, nullptr,
+                                           nullptr, y, inv_rms, width, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_head_rms_norm_forward launch");
+  return ATTNRES_OK;
+}
+
+int attnres_head_rms_norm_backward(int64_t rows, int width, int num_heads, int dtype, const void* grad_y,
+                                   const void* x, int64_t x_row_stride, const float* inv_rms, void* grad_x,
+                                   int64_t grad_x_row_stride, void* stream) {
+  if (rows < 0 || width < 1 || num_heads < 1 || width % num_heads)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "head rms norm: width must divide by num_heads");
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (grad_x_row_stride < width || x_row_stride < width)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "head rms norm: a row stride < width");
+  if (rows > 0 && (!grad_y || !x || !inv_rms || !grad_x))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "head rms norm backward: NULL buffer");
+  cudaError_t e = attnres::headnorm_launch(true, dtype, rows, width, num_heads, grad_y, x_row_stride, 0.f, x,
+                                           inv_rms, grad_x, nullptr, grad_x_row_stride,
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_head_rms_norm_backward launch");
+  return ATTNRES_OK;
+}
+
 int attnres_phase1_forward(int num_sources, int num_queries, int64_t num_tokens, int value_dim, int dtype,
                            const void* const* values, const int64_t* value_row_strides, const void* logits,
                            int logit_dtype, int output_norm, float output_eps, void* output, float* lse,

@@ -177,6 +177,11 @@ cudaError_t phase2_run(bool bwd, int mode, long long N, int d, int R, int dtype,
                        void* dkey, float* dlogit, void* dprev, float* dlse, float* grad_query, float* grad_bias,
                        void* workspace, cudaStream_t st);
 
+// Per-head key RMS norm (headnorm.cu).
+cudaError_t headnorm_launch(bool bwd, int dtype, long long rows, int width, int heads, const void* a, long long as,
+                            float eps, const void* b, const float* inv_in, void* out, float* inv_out, long long os,
+                            cudaStream_t st);
+
 // Block summary (summary.cu).
 int summary_bwd_grid(long long n);
 cudaError_t summary_forward_launch(long long n, int dtype, const void* partial, const void* x,

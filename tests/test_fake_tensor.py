@@ -35,6 +35,8 @@ def test_fake_shapes_of_all_ops():
         assert po.shape == (Q, B, T, D) and lse.shape == (Q, B, T)
         bo, binv = ops.base_read(v, _fake(mode, D), None, True, True)
         assert bo.shape == (B, T, D) and binv.shape == (B * T,)
+        fo, fk, fq, fi = ops.lrid_fused_projection(v[0], _fake(mode, D + R + R, D), D, R, H, True, R)
+        assert fo.shape == (B, T, D) and fk.shape == (B, T, R) and fq.shape == (B, T, R) and fi.shape == (B * T, H)
         ssum, ssrc = ops.block_summary(v[0], v[1], None, 0.5)
         assert ssum.shape == (B, T, D) and ssrc.shape == (B, T, D)
         p2o, p2i = ops.phase2(0, v[0], k[0], None, _fake(mode, R), v[1], _fake(mode, B, T, dtype=torch.float32),
