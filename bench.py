@@ -55,6 +55,7 @@ def parse():
     p.add_argument("--config", choices=sorted(CONFIGS), default="config2")
     p.add_argument("--e2e-steps", type=int, default=12)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-aux", action="store_true", help="skip the config-3/4 and secondary measurements")
     p.add_argument("--profile", action="store_true",
                    help="short run for ncu: warmup + steps eager launches, no e2e/cpu legs")
     return p.parse_args()
@@ -137,6 +138,8 @@ def cpu_oracle_rate(c, target_s=12.0, max_tokens=4096):
     """cpu_baseline leg: the oracle's fwd+bwd rate on a bounded token sample."""
     from oracle import oracle
 
+    oracle.set_num_threads(len(os.sched_getaffinity(0)))
+
     n = min(max_tokens, c["B"] * c["T"])
     v, k, g, kw = _oracle_inputs(c, n)
     tokens, t0 = 0, time.perf_counter()
@@ -173,6 +176,9 @@ def run_reference(args, c):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; the reference arm runs on
+    # rank 0 alone and takes every host core it may run on
+    oracle.set_num_threads(len(os.sched_getaffinity(0)))
     H = c["H"]
     v, k, g, kw = _oracle_inputs(c, 256)
     t0 = time.perf_counter()
@@ -250,6 +256,140 @@ def make_inputs(c, device, torch, seed):
     return x
 
 
+def measure(name, c, steps, warmup, torch, ops, device, world, rank, stream, comm, seed=1234):
+    """Times `steps` fwd+bwd steps of config `c` on this rank, after `warmup`.
+
+    Steps are captured U at a time in one CUDA graph. At N > 1 each step's
+    NCCL all-reduce of the summed parameter gradients (query, gate, W_k) is
+    captured on a second stream, overlapping the next step's forward; the next
+    backward, which rewrites the gradients, waits for it. The forward and the
+    backward are also timed alone (graphs of one launch each) for the
+    per-kernel rooflines. Returns max-over-ranks step, forward and backward
+    times."""
+    x = make_inputs(c, device, torch, seed=seed + rank)
+    H, scale = c["H"], c["scale"]
+    q, gate, qdyn = x["query"], x["gate"], x["qdyn"]
+    kv = bool(c.get("kv"))
+
+    def fwd():
+        if kv:
+            return ops.lrid_kv_read(x["values"], x["weight"], q, gate, qdyn, None, H, scale, True, 0, True)
+        return ops.lrid_read(x["values"], x["keys"], q, gate, qdyn, None, H, scale, True, 0)
+
+    def bwd(*fo):
+        if kv:
+            out, inv, keys, vinv, alpha = fo
+            r = ops.lrid_kv_read_backward(x["values"], x["weight"], keys, vinv, alpha, q, gate, qdyn, None,
+                                          x["grad"], out, inv, H, scale, True, 0, True)
+            # (dV, dW, dq, dgate, ...): the summed parameter gradients are dW, dq, dgate
+            return [r[1], r[2]] + ([r[3]] if qdyn is not None else [])
+        r = ops.lrid_read_backward(x["values"], x["keys"], q, gate, qdyn, None, x["grad"], fo[0], fo[1],
+                                   H, scale, True, 0)
+        return [r[2]] + ([r[3]] if qdyn is not None else [])
+
+    from attnres_b200.sharding import allreduce_param_grads
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):  # allocator warm-up outside capture
+            grads = bwd(*fwd())
+        if world > 1:
+            allreduce_param_grads(grads)  # communicator warm-up
+    torch.cuda.synchronize()
+
+    # U steps per graph replay (steps % U == 0), so that consecutive kernels
+    # of the timed loop launch inside one graph
+    U = next(u for u in (10, 8, 5, 4, 2, 1) if steps % u == 0 and warmup % u == 0)
+
+    def body(n):
+        prev = None
+        for _ in range(n):
+            fo = fwd()
+            if prev is not None:
+                stream.wait_event(prev)  # the all-reduce of the previous step has read its gradients
+            grads = bwd(*fo)
+            if world > 1:
+                # the all-reduce of this step overlaps the next step's forward
+                ready = torch.cuda.Event()
+                ready.record(stream)
+                comm.wait_event(ready)
+                with torch.cuda.stream(comm):
+                    allreduce_param_grads(grads)
+                    prev = torch.cuda.Event()
+                    prev.record(comm)
+        if prev is not None:
+            stream.wait_event(prev)
+
+    g_step = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step, stream=stream):
+        body(U)
+    # forward / backward alone, for the per-kernel rooflines
+    g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_fwd, stream=stream):
+        fo = fwd()
+    with torch.cuda.graph(g_bwd, stream=stream):
+        bwd(*fo)
+    torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup // U):
+            g_step.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps // U):
+            g_step.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    # per-kernel times: each graph replayed back to back, events on its stream
+    nk = max(20, min(steps, 200))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g_fwd.replay()
+            g_bwd.replay()
+        ev[0].record(stream)
+        for _ in range(nk):
+            g_fwd.replay()
+        ev[1].record(stream)
+        ev[2].record(stream)
+        for _ in range(nk):
+            g_bwd.replay()
+        ev[3].record(stream)
+    torch.cuda.synchronize()
+    fwd_ms = ev[0].elapsed_time(ev[1]) / nk
+    bwd_ms = ev[2].elapsed_time(ev[3]) / nk
+    t = torch.tensor([ms, fwd_ms, bwd_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, fwd_ms, bwd_ms = (float(v) for v in t.tolist())
+    del g_step, g_fwd, g_bwd, fo, grads
+    return x, {"ms": ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "steps_per_graph": U}
+
+
+def rooflines(c, t, hbm, world):
+    """Tokens/s and HBM fractions of one measured config (algorithmic bytes)."""
+    tokens = c["B"] * c["T"]
+    fwd_b, bwd_b = algorithmic_bytes(c)
+    return {
+        "tokens_per_s": tokens * world / (t["ms"] * 1e-3), "ms_per_step": t["ms"],
+        "fwd_kernel_ms": t["fwd_ms"], "bwd_kernel_ms": t["bwd_ms"],
+        "fwd_gbs": tokens * fwd_b / (t["fwd_ms"] * 1e-3) / 1e9,
+        "bwd_gbs": tokens * bwd_b / (t["bwd_ms"] * 1e-3) / 1e9,
+        "step_gbs": tokens * (fwd_b + bwd_b) / (t["ms"] * 1e-3) / 1e9,
+        "fwd_frac": tokens * fwd_b / (t["fwd_ms"] * 1e-3) / 1e9 / hbm,
+        "bwd_frac": tokens * bwd_b / (t["bwd_ms"] * 1e-3) / 1e9 / hbm,
+        "step_frac": tokens * (fwd_b + bwd_b) / (t["ms"] * 1e-3) / 1e9 / hbm,
+        "algorithmic_bytes_per_token": {"fwd": fwd_b, "bwd": bwd_b},
+    }
+
+
 def main():
     args = parse()
     c = CONFIGS[args.config]
@@ -270,129 +410,31 @@ def main():
     import attnres_b200  # noqa: F401  (registers torch.ops.attnres.*)
 
     ops = torch.ops.attnres
-    x = make_inputs(c, device, torch, seed=1234 + rank)
-    H, scale = c["H"], c["scale"]
-    gated = c["query"] == "gated"
-    q, gate, qdyn = x["query"], x["gate"], x["qdyn"]
-
     kv = bool(c.get("kv"))
-
-    def fwd():
-        if kv:
-            return ops.lrid_kv_read(x["values"], x["weight"], q, gate, qdyn, None, H, scale, True, 0, True)
-        return ops.lrid_read(x["values"], x["keys"], q, gate, qdyn, None, H, scale, True, 0)
-
-    def bwd(*fo):
-        if kv:
-            out, inv, keys, vinv, alpha = fo
-            r = ops.lrid_kv_read_backward(x["values"], x["weight"], keys, vinv, alpha, q, gate, qdyn, None,
-                                          x["grad"], out, inv, H, scale, True, 0, True)
-            # (dV, dW, dq, dgate, ...) -> keep dq / dgate at the same positions as the plain read
-            return r[0], r[1], r[2], r[3]
-        out, inv = fo
-        return ops.lrid_read_backward(x["values"], x["keys"], q, gate, qdyn, None, x["grad"], out, inv,
-                                      H, scale, True, 0)
-
-    from attnres_b200.sharding import allreduce_param_grads
-
-    def allreduce(dq, dgate):
-        # the only cross-GPU step: one bucketed NCCL all-reduce of the summed grads
-        if world > 1:
-            allreduce_param_grads([dq] + ([dgate] if gated else []) + ([dw] if kv else []))
-
+    gated = c["query"] == "gated"
     stream = torch.cuda.Stream(device)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    comm = torch.cuda.Stream(device)
 
     if args.profile:
+        x = make_inputs(c, device, torch, seed=1234 + rank)
+        H, scale = c["H"], c["scale"]
         with torch.cuda.stream(stream):
             for _ in range(args.warmup + args.steps):
-                bwd(*fwd())
+                if kv:
+                    out, inv, keys, vinv, alpha = ops.lrid_kv_read(x["values"], x["weight"], x["query"], None,
+                                                                   None, None, H, scale, True, 0, True)
+                    ops.lrid_kv_read_backward(x["values"], x["weight"], keys, vinv, alpha, x["query"], None, None,
+                                              None, x["grad"], out, inv, H, scale, True, 0, True)
+                else:
+                    out, inv = ops.lrid_read(x["values"], x["keys"], x["query"], x["gate"], x["qdyn"], None, H,
+                                             scale, True, 0)
+                    ops.lrid_read_backward(x["values"], x["keys"], x["query"], x["gate"], x["qdyn"], None,
+                                           x["grad"], out, inv, H, scale, True, 0)
         torch.cuda.synchronize()
         if rank == 0:
             print(json.dumps({"profile_run": True, "config": args.config}), flush=True)
         return
 
-    # ---- capture fwd and bwd as two CUDA graphs (static buffers) ----------
-    with torch.cuda.stream(stream):
-        for _ in range(3):  # allocator warm-up outside capture
-            res = bwd(*fwd())
-    torch.cuda.synchronize()
-    g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_fwd, stream=stream):
-        fo = fwd()
-    with torch.cuda.graph(g_bwd, stream=stream):
-        res = bwd(*fo)
-    dq, dgate = res[2], res[3]
-    dw = res[1] if kv else None
-    torch.cuda.synchronize()
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    # The gradient all-reduce of step k runs on its own stream, overlapping the
-    # forward of step k+1 (which does not read it); the backward of step k+1,
-    # which rewrites the gradient buffers, waits for it.
-    comm = torch.cuda.Stream(device)
-    bwd_done = [torch.cuda.Event() for _ in range(2)]
-    comm_done = [torch.cuda.Event() for _ in range(2)]
-
-    def step(i, fe=None, be=None):
-        if fe:
-            fe[0].record(stream)
-        g_fwd.replay()
-        if fe:
-            fe[1].record(stream)
-        if world > 1 and i > 0:
-            stream.wait_event(comm_done[(i - 1) % 2])
-        if be:
-            be[0].record(stream)
-        g_bwd.replay()
-        if be:
-            be[1].record(stream)
-        if world > 1:
-            bwd_done[i % 2].record(stream)
-            comm.wait_event(bwd_done[i % 2])
-            with torch.cuda.stream(comm):
-                allreduce(dq, dgate)
-                comm_done[i % 2].record(comm)
-
-    def drain(last):
-        if world > 1:
-            stream.wait_event(comm_done[last % 2])
-
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            step(i)
-        drain(args.warmup - 1)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    # per-kernel CUDA-event timing on the launching stream
-    fwd_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps)]
-    bwd_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps)]
-    with torch.cuda.stream(stream):
-        ev[0].record(stream)
-        for i in range(args.steps):
-            step(i, fwd_events[i], bwd_events[i])
-        drain(args.steps - 1)
-        ev[1].record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop()
-    ms = ev[0].elapsed_time(ev[1]) / args.steps
-    fwd_ms = float(np.mean([a.elapsed_time(b) for a, b in fwd_events]))
-    bwd_ms = float(np.mean([a.elapsed_time(b) for a, b in bwd_events]))
-    t = torch.tensor([ms, fwd_ms, bwd_ms], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, fwd_ms, bwd_ms = (float(v) for v in t.tolist())
-
-    tokens = c["B"] * c["T"]
-    value = tokens * world / (ms * 1e-3)
-    fwd_b, bwd_b = algorithmic_bytes(c)
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -400,8 +442,18 @@ def main():
     except Exception:
         pass
     hbm = float(peaks.get("hbm_gbs", 6650.0))
-    traffic = profiled_traffic_per_token()
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    x, t = measure(args.config, c, args.steps, args.warmup, torch, ops, device, world, rank, stream, comm)
+    clocks = sampler.stop()
+    ms, fwd_ms, bwd_ms = t["ms"], t["fwd_ms"], t["bwd_ms"]
+
+    tokens = c["B"] * c["T"]
+    value = tokens * world / (ms * 1e-3)
+    fwd_b, bwd_b = algorithmic_bytes(c)
+    traffic = profiled_traffic_per_token()
     bwd_gbs = tokens * bwd_b / (bwd_ms * 1e-3) / 1e9
     fwd_gbs = tokens * fwd_b / (fwd_ms * 1e-3) / 1e9
     step_gbs = tokens * (fwd_b + bwd_b) / (ms * 1e-3) / 1e9
@@ -413,113 +465,23 @@ def main():
 
     proj = None
     if kv:
-        # the tcgen05 key projection alone, for its TFLOP/s against the tensor peak
-        from attnres_b200.ops import _kv_project
+        proj = projection_rate(c, x, stream, torch, peaks, hbm)
+    del x
+    torch.cuda.empty_cache()
 
-        with torch.cuda.stream(stream):
-            _kv_project(x["values"], x["weight"], True)
-        torch.cuda.synchronize()
-        g_proj = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_proj, stream=stream):
-            _kv_project(x["values"], x["weight"], True)
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            g_proj.replay()
-            p0.record(stream)
-            for _ in range(10):
-                g_proj.replay()
-            p1.record(stream)
-        torch.cuda.synchronize()
-        pms = p0.elapsed_time(p1) / 10
-        flops = 2.0 * c["S"] * tokens * c["D"] * c["R"]
-        tpeak = float(peaks.get("bf16_tflops", 1590.0))
-        pbytes = c["S"] * tokens * (c["D"] + c["R"]) * 2
-        proj = {"kernel": "keyproj_tc_kernel (tcgen05)", "ms": pms, "tflops": flops / pms / 1e9,
-                "peak_tflops": tpeak, "frac_tensor": flops / pms / 1e9 / tpeak,
-                "gbs": pbytes / pms / 1e6, "frac_hbm": pbytes / pms / 1e6 / hbm}
-
-    # a9: the block-summary op (running block sum + scaled source) on rows of
-    # this config, 4x its token count so the four arrays (537 MB at config 2)
-    # are far larger than L2
     aux = None
-    if not kv:
-        xs = torch.randn(4 * c["B"], c["T"], c["D"], device=device, dtype=torch.bfloat16)
-        ps = torch.randn_like(xs)
-        bsum = torch.ops.attnres.block_summary
-        with torch.cuda.stream(stream):
-            bsum(ps, xs, None, 0.25)
-        torch.cuda.synchronize()
-        g_sum = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_sum, stream=stream):
-            bsum(ps, xs, None, 0.25)
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                g_sum.replay()
-            s0.record(stream)
-            for _ in range(20):
-                g_sum.replay()
-            s1.record(stream)
-        torch.cuda.synchronize()
-        sms = s0.elapsed_time(s1) / 20
-        sbytes = 4 * xs.numel() * 2
-        aux = {"block_summary": {"kernel": "summary_fwd_kernel (a9: sum = partial + x, source = sum * c)",
-                                 "elements": xs.numel(), "ms": sms, "achieved_gbs": sbytes / sms / 1e6,
-                                 "frac": sbytes / sms / 1e6 / hbm, "bytes": sbytes}}
-        # cached-logit phase 2 (LRID key, one query) on the same 4x rows: forward
-        # and backward, each timed alone
-        R = c["R"]
-        pk = torch.randn(xs.shape[0], xs.shape[1], R, device=device, dtype=torch.bfloat16)
-        q2 = torch.randn(R, device=device, dtype=torch.bfloat16) * 0.1
-        lse2 = torch.randn(xs.shape[0], xs.shape[1], device=device)
-        p2 = torch.ops.attnres.phase2
-        p2b = torch.ops.attnres.phase2_backward
-
-        def p2f():
-            return p2(0, ps, pk, None, q2, xs, lse2, c["scale"], True, None, 0.0, False)
-
-        def p2g(o):
-            return p2b(0, ps, pk, None, q2, xs, lse2, c["scale"], True, None, 0.0, False, o[0], o[1], ps, True,
-                       False)
-
-        with torch.cuda.stream(stream):
-            o2 = p2f()
-            p2g(o2)
-        torch.cuda.synchronize()
-        gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gf, stream=stream):
-            o2 = p2f()
-        with torch.cuda.graph(gb, stream=stream):
-            p2g(o2)
-        ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                gf.replay()
-                gb.replay()
-            ev2[0].record(stream)
-            for _ in range(10):
-                gf.replay()
-            ev2[1].record(stream)
-            for _ in range(10):
-                gb.replay()
-            ev2[2].record(stream)
-        torch.cuda.synchronize()
-        fms, bms = ev2[0].elapsed_time(ev2[1]) / 10, ev2[1].elapsed_time(ev2[2]) / 10
-        ntok = xs.shape[0] * xs.shape[1]
-        fb = ntok * (3 * c["D"] + R) * 2 + ntok * 4
-        bb = ntok * (5 * c["D"] + 2 * R) * 2 + ntok * 8
-        aux["phase2"] = {"kernel": "phase2_fwd_kernel / phase2_bwd_kernel (LRID key, key norm)", "tokens": ntok,
-                         "fwd_ms": fms, "fwd_frac": fb / fms / 1e6 / hbm, "bwd_ms": bms,
-                         "bwd_frac": bb / bms / 1e6 / hbm, "fwd_bytes": fb, "bwd_bytes": bb}
-        del xs, ps, pk, o2
+    if args.config == "config2" and not args.no_aux:
+        aux = aux_measurements(c, stream, comm, torch, ops, device, world, rank, hbm, peaks)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not kv:
         r, cores, sample = cpu_oracle_rate(c, target_s=12.0)
         cpu = {"value": r, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
-    # per step: forward kernel, backward kernel, fixed-order reduce of dq (+ dgate)
-    launches_per_step = 3 + (1 if gated else 0)
+    # per step: the forward and the backward kernel (the backward's last CTA
+    # sums the parameter gradients); the key-from-value step adds the
+    # projection and its backward's prepass and weight-gradient sum
+    launches_per_step = 5 if kv else 2
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -547,6 +509,180 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def projection_rate(c, x, stream, torch, peaks, hbm):
+    """The tcgen05 key projection alone, for its TFLOP/s against the tensor peak."""
+    from attnres_b200.ops import _kv_project
+
+    tokens = c["B"] * c["T"]
+    with torch.cuda.stream(stream):
+        _kv_project(x["values"], x["weight"], True)
+    torch.cuda.synchronize()
+    g_proj = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_proj, stream=stream):
+        _kv_project(x["values"], x["weight"], True)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        g_proj.replay()
+        p0.record(stream)
+        for _ in range(10):
+            g_proj.replay()
+        p1.record(stream)
+    torch.cuda.synchronize()
+    pms = p0.elapsed_time(p1) / 10
+    flops = 2.0 * c["S"] * tokens * c["D"] * c["R"]
+    tpeak = float(peaks.get("bf16_tflops", 1590.0))
+    pbytes = c["S"] * tokens * (c["D"] + c["R"]) * 2
+    return {"kernel": "keyproj_tc_kernel (tcgen05)", "ms": pms, "tflops": flops / pms / 1e9,
+            "peak_tflops": tpeak, "frac_tensor": flops / pms / 1e9 / tpeak,
+            "gbs": pbytes / pms / 1e6, "frac_hbm": pbytes / pms / 1e6 / hbm}
+
+
+def aux_measurements(c, stream, comm, torch, ops, device, world, rank, hbm, peaks):
+    """Secondary lines of the default run, each timed like the headline step:
+    BASELINE configs 3 and 4 (config 4 all-reduces dW_k and dq at N > 1), the
+    model's default read (output RMS norm, count-prior logit biases) at the
+    config-2 shape, the block summary and the cached-logit phase 2."""
+    aux = {}
+    for name, steps, warm in (("config3", 100, 10), ("config4", 20, 5)):
+        cc = CONFIGS[name]
+        x, t = measure(name, cc, steps, warm, torch, ops, device, world, rank, stream, comm)
+        r = rooflines(cc, t, hbm, world)
+        if cc.get("kv"):
+            r["projection"] = projection_rate(cc, x, stream, torch, peaks, hbm)
+            r["note"] = ("algorithmic bytes read V once per direction; the step reads V twice per direction "
+                         "(projection, then read)")
+        r["workload"] = config_block(cc, argparse.Namespace(config=name, gpus=world))["workload"]
+        aux[name] = r
+        del x
+        torch.cuda.empty_cache()
+    aux["config2_model_read"] = model_read_rate(c, stream, torch, ops, device, rank, hbm)
+    aux.update(block_summary_and_phase2(c, stream, torch, device, hbm))
+    return aux
+
+
+def model_read_rate(c, stream, torch, ops, device, rank, hbm):
+    """The read that model.py issues by default (attnres_fuse_read_norm=True and
+    the count prior, model.py:90, :2238-2244): output RMS norm per head and
+    per-source logit biases, at the config-2 shape, fwd+bwd."""
+    x = make_inputs(c, device, torch, seed=99 + rank)
+    H, scale = c["H"], c["scale"]
+    bias = torch.log(torch.arange(1, c["S"] + 1, device=device, dtype=torch.float32))
+
+    def fwd():
+        return ops.lrid_read(x["values"], x["keys"], x["query"], None, None, bias, H, scale, True, 1)
+
+    def bwd(fo):
+        return ops.lrid_read_backward(x["values"], x["keys"], x["query"], None, None, bias, x["grad"], fo[0],
+                                      fo[1], H, scale, True, 1)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            bwd(fwd())
+    torch.cuda.synchronize()
+    gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gf, stream=stream):
+        fo = fwd()
+    with torch.cuda.graph(gb, stream=stream):
+        bwd(fo)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    n = 200
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            gf.replay()
+            gb.replay()
+        ev[0].record(stream)
+        for _ in range(n):
+            gf.replay()
+            gb.replay()
+        ev[1].record(stream)
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / n
+    tokens = c["B"] * c["T"]
+    fwd_b, bwd_b = algorithmic_bytes(c)
+    # the norm adds the normed output read in the backward and the inverse rms
+    fwd_b, bwd_b = fwd_b + 4, bwd_b + c["D"] * 2 + 4
+    return {"what": "LRID read with output RMS norm (per head) and count-prior logit biases, config-2 shape",
+            "tokens_per_s": tokens / (ms * 1e-3), "ms_per_step": ms,
+            "step_frac": tokens * (fwd_b + bwd_b) / (ms * 1e-3) / 1e9 / hbm,
+            "algorithmic_bytes_per_token": {"fwd": fwd_b, "bwd": bwd_b}}
+
+
+def block_summary_and_phase2(c, stream, torch, device, hbm):
+    """a9 block summary (running block sum + scaled source) and the cached-logit
+    phase 2 (LRID key, one query) on rows of this config, 4x its token count so
+    that the arrays (537 MB for the summary at config 2) are far larger than L2."""
+    aux = {}
+    xs = torch.randn(4 * c["B"], c["T"], c["D"], device=device, dtype=torch.bfloat16)
+    ps = torch.randn_like(xs)
+    bsum = torch.ops.attnres.block_summary
+    with torch.cuda.stream(stream):
+        bsum(ps, xs, None, 0.25)
+    torch.cuda.synchronize()
+    g_sum = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_sum, stream=stream):
+        bsum(ps, xs, None, 0.25)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g_sum.replay()
+        s0.record(stream)
+        for _ in range(20):
+            g_sum.replay()
+        s1.record(stream)
+    torch.cuda.synchronize()
+    sms = s0.elapsed_time(s1) / 20
+    sbytes = 4 * xs.numel() * 2
+    aux["block_summary"] = {"kernel": "summary_fwd_kernel (a9: sum = partial + x, source = sum * c)",
+                            "elements": xs.numel(), "ms": sms, "achieved_gbs": sbytes / sms / 1e6,
+                            "frac": sbytes / sms / 1e6 / hbm, "bytes": sbytes}
+    R = c["R"]
+    pk = torch.randn(xs.shape[0], xs.shape[1], R, device=device, dtype=torch.bfloat16)
+    q2 = torch.randn(R, device=device, dtype=torch.bfloat16) * 0.1
+    lse2 = torch.randn(xs.shape[0], xs.shape[1], device=device)
+    p2 = torch.ops.attnres.phase2
+    p2b = torch.ops.attnres.phase2_backward
+
+    def p2f():
+        return p2(0, ps, pk, None, q2, xs, lse2, c["scale"], True, None, 0.0, False)
+
+    def p2g(o):
+        return p2b(0, ps, pk, None, q2, xs, lse2, c["scale"], True, None, 0.0, False, o[0], o[1], ps, True,
+                   False)
+
+    with torch.cuda.stream(stream):
+        o2 = p2f()
+        p2g(o2)
+    torch.cuda.synchronize()
+    gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gf, stream=stream):
+        o2 = p2f()
+    with torch.cuda.graph(gb, stream=stream):
+        p2g(o2)
+    ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            gf.replay()
+            gb.replay()
+        ev2[0].record(stream)
+        for _ in range(10):
+            gf.replay()
+        ev2[1].record(stream)
+        for _ in range(10):
+            gb.replay()
+        ev2[2].record(stream)
+    torch.cuda.synchronize()
+    fms, bms = ev2[0].elapsed_time(ev2[1]) / 10, ev2[1].elapsed_time(ev2[2]) / 10
+    ntok = xs.shape[0] * xs.shape[1]
+    fb = ntok * (3 * c["D"] + R) * 2 + ntok * 4
+    bb = ntok * (5 * c["D"] + 2 * R) * 2 + ntok * 8
+    aux["phase2"] = {"kernel": "phase2_fwd_kernel / phase2_bwd_kernel (LRID key, key norm)", "tokens": ntok,
+                     "fwd_ms": fms, "fwd_frac": fb / fms / 1e6 / hbm, "bwd_ms": bms,
+                     "bwd_frac": bb / bms / 1e6 / hbm, "fwd_bytes": fb, "bwd_bytes": bb}
+    del xs, ps, pk, o2
+    torch.cuda.empty_cache()
+    return aux
 
 
 def run_e2e(args, c, x, device, torch, dist, world):

@@ -32,6 +32,11 @@ def allreduce_param_grads(grads: Sequence[torch.Tensor], group=None) -> None:
     grads = [g for g in grads if g is not None]
     if not grads or not dist.is_initialized() or dist.get_world_size(group) == 1:
         return
+    if all(g.dtype == torch.float32 and g.is_contiguous() for g in grads) and len(grads) <= 2:
+        # already fp32: reduce in place, no packing copies
+        for g in grads:
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=group)
+        return
     flat = torch.cat([g.reshape(-1).to(torch.float32) for g in grads])
     dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
     offset = 0

@@ -103,14 +103,17 @@ def lrid_attention_residual_phase2_torch(partial_value: Tensor, partial_key: Ten
                                          interblock_output: Tensor, interblock_lse: Tensor, logit_scale: float,
                                          key_norm: bool, normalize_output: bool = False,
                                          logit_bias=0.0) -> Tensor:
-    """attnres_ops.py:4142-4160."""
+    """attnres_ops.py:4142-4160. Unlike the base and given-logit merges (addcmul,
+    :2642 and :4071), the LRID merge is a torch.lerp (:4159), which rounds
+    differently in 16-bit dtypes."""
     query = query.reshape(-1).to(partial_key.dtype)
     partial_key = partial_key.reshape(partial_key.size(0), partial_key.size(1), -1)
     key = _norm(partial_key.float()).to(partial_value.dtype) if key_norm else partial_key
     logit = torch.sum(key * query.to(key.dtype).view(1, 1, -1), dim=-1) * float(logit_scale)
     logit = _add_bias(logit.float(), logit_bias)
-    return attention_residual_phase2_from_logit(partial_value, logit, interblock_output, interblock_lse,
-                                                normalize_output=normalize_output)
+    prob = torch.sigmoid(logit.float() - interblock_lse.float()).to(partial_value.dtype)
+    out = torch.lerp(interblock_output, partial_value, prob.unsqueeze(-1))
+    return _norm(out) if normalize_output else out
 
 
 def lrid_attention_residual_phase2(partial_value: Tensor, partial_key: Tensor, query: Tensor,

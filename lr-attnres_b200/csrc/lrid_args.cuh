@@ -37,9 +37,14 @@ struct LridArgs {
   float* partials;
   int part_stride;
   int want_bias_grad;
-  // Streaming kernels: {next token, finished warps} counter pair for the
-  // dynamic token schedule; null selects the static round-robin schedule.
-  unsigned long long* claim;
+  // Streaming forward: this launch's counter slot {next token, finished
+  // warps}; null selects the static round-robin token schedule.
+  unsigned long long* sched;
+  int dynamic_tokens;  // take tokens from sched[0]
+  // Test hook: CTA 0 / warp 0 posts the byte count of its `withhold`-th unit
+  // but issues no copy, so its wait runs out after wait_ns (-1: off).
+  long long withhold;
+  unsigned long long wait_ns;
   TmaLayout tma;
 };
 

@@ -26,7 +26,10 @@ constexpr size_t kNoallocScratchBytes = 4u << 20;  // 4 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
 std::mutex g_mu;
-std::unordered_map<int, void*> g_addr;  // device ordinal -> device address of the scratch
+// device ordinal -> device address of the scratch. The cache assumes the
+// device's primary context lives as long as the process: after a
+// cudaDeviceReset the module is loaded again and the cached address is stale.
+std::unordered_map<int, void*> g_addr;
 
 // Looks up the scratch's device address once per device (that device current).
 int scratch_address(void** out) {
@@ -64,12 +67,15 @@ int attnres_lrid_backward_noalloc(int num_sources, int64_t num_tokens, int value
                                   const float* output_inv_rms, void* const* grad_values,
                                   void* const* grad_keys, void* grad_query, float* grad_query_gate,
                                   void* grad_query_dynamic, float* grad_logit_bias, void* stream) {
+  // A per-token query with no logit-bias gradient has no parameter gradient
+  // to sum: that call uses no scratch, whatever its size.
+  const bool uses_scratch = query_mode != ATTNRES_QUERY_DYNAMIC || grad_logit_bias != nullptr;
   const size_t need = attnres_lrid_backward_workspace_bytes(num_sources, num_tokens, value_dim, key_dim,
                                                             num_heads, dtype);
-  if (need == 0)
+  if (need == 0 && uses_scratch)
     return attnres::record_error(ATTNRES_ERR_INVALID_ARGUMENT,
                                  "attnres_lrid_backward_noalloc: invalid geometry or no CUDA device");
-  if (need > kNoallocScratchBytes) {
+  if (uses_scratch && need > kNoallocScratchBytes) {
     char msg[200];
     snprintf(msg, sizeof(msg),
              "attnres_lrid_backward_noalloc: this geometry needs %zu bytes of scratch, more than the "

@@ -157,7 +157,10 @@ def test_lrid_dtypes_and_query_modes(dtype, query_kind):
 
 @pytest.mark.parametrize("name,S,D,R,H,scale,query_kind,norm", [
     ("config2_lrid_h1", 9, 1024, 64, 1, 1 / 8, "static", False),
+    ("config2_lrid_h1_outnorm", 9, 1024, 64, 1, 1 / 8, "static", True),
     ("config3_gated_h4", 13, 2048, 64, 4, 1 / 4, "gated", False),
+    ("config3_gated_h4_outnorm", 13, 2048, 64, 4, 1 / 4, "gated", True),
+    ("model_h2_outnorm", 13, 1024, 64, 2, 1 / 4, "static", True),
     ("sources17", 17, 512, 64, 2, 0.25, "static", True),
     ("sources64", 64, 128, 32, 1, 0.25, "static", False),
     ("heads3", 5, 96, 24, 3, 0.5, "static", True),
@@ -351,3 +354,79 @@ def test_lrid_forward_token_schedule_static_equals_dynamic(kernel_path, monkeypa
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, ref)
+
+
+def test_lrid_graph_replays_and_eager_launches_on_two_streams(kernel_path):
+    """Forward and backward captured in a CUDA graph replay on one stream while
+    eager launches of other inputs run on a second stream, many times over:
+    each captured launch owns its token / CTA counters, so neither side skips
+    or repeats rows. Results must equal the launches run alone, bit for bit
+    (the backward's parameter-gradient sums have a fixed order)."""
+    if kernel_path != "auto":
+        pytest.skip("counter slots belong to the streaming kernels (auto path)")
+    ops = torch.ops.attnres
+    _ops()
+    S, N, D, R, H = 9, 5000, 1024, 64, 1
+    torch.manual_seed(7)
+
+    def make():
+        v = [torch.randn(1, N, D, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
+        k = [torch.randn(1, N, R, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
+        g = torch.randn(1, N, D, device="cuda", dtype=torch.bfloat16)
+        return v, k, g
+
+    q = (torch.randn(H, R // H, device="cuda") * 0.02).to(torch.bfloat16)
+    a, b = make(), make()
+
+    def step(x):
+        v, k, g = x
+        out, inv = ops.lrid_read(v, k, q, None, None, None, H, 0.125, True, 0)
+        res = ops.lrid_read_backward(v, k, q, None, None, None, g, out, inv, H, 0.125, True, 0)
+        return out, res[2], res[0][4]
+
+    ref_a, ref_b = step(a), step(b)
+    sa, sb = torch.cuda.Stream(), torch.cuda.Stream()
+    with torch.cuda.stream(sa):
+        step(a)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=sa):
+        got_a = step(a)
+    torch.cuda.synchronize()
+    for _ in range(40):
+        with torch.cuda.stream(sa):
+            graph.replay()
+        with torch.cuda.stream(sb):
+            got_b = step(b)
+        torch.cuda.synchronize()
+        for x, y in zip(got_a, ref_a):
+            assert torch.equal(x, y)
+        for x, y in zip(got_b, ref_b):
+            assert torch.equal(x, y)
+
+
+def test_lrid_output_norm_read_matches_the_unnormed_read_then_rms_norm(kernel_path):
+    """The model's default read (normalize_output with H == 1, model.py:2238-2244)
+    against the composition it fuses: the plain read, then F.rms_norm of the
+    value-dtype output, at the config-2 row shape."""
+    ops = _ops()
+    S, B, T, D, R, H = 9, 2, 1500, 1024, 64, 1
+    torch.manual_seed(11)
+    values = [torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
+    keys = [torch.randn(B, T, R, device="cuda", dtype=torch.bfloat16) for _ in range(S)]
+    q = torch.randn(H, R // H, device="cuda") * 0.02
+    g = torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16)
+    grads = []
+    for fused in (True, False):
+        vs = [v.clone().requires_grad_(True) for v in values]
+        ks = [k.clone().requires_grad_(True) for k in keys]
+        qq = q.clone().requires_grad_(True)
+        if fused:
+            out = ops.lrid_attention_residual_read(vs, ks, qq, H, 0.125, True, normalize_output=True)
+        else:
+            out = ops.lrid_attention_residual_read(vs, ks, qq, H, 0.125, True)
+            out = torch.nn.functional.rms_norm(out.float(), (D,), eps=float(torch.finfo(torch.bfloat16).eps))
+        out.float().backward(g.float())
+        grads.append((out.float(), qq.grad.float(), vs[2].grad.float(), ks[6].grad.float()))
+    for name, x, y in zip(("out", "dq", "dV2", "dK6"), *grads):
+        assert_close(name, to_np(x), to_np(y), torch.bfloat16, sum_terms=B * T if name == "dq" else 1)

@@ -104,3 +104,48 @@ def test_noalloc_rejects_geometries_beyond_the_static_scratch():
         ctypes.c_void_p(one.data_ptr()), None, None, None, None)
     assert rc == 2
     assert "static scratch" in L.attnres_last_error().decode()
+
+
+def test_noalloc_accepts_calls_that_use_no_scratch():
+    """A per-token (dynamic) query without a logit-bias gradient sums no
+    parameter gradient, so the call uses no scratch: a geometry whose
+    workspace would exceed the static array still runs, and matches the
+    workspace entry point (which needs no workspace for it either)."""
+    L = N.load()
+    S, d, R, H = 64, 512, 4096, 8  # key heads of 512: the widest the kernels take
+    cap = L.attnres_noalloc_scratch_bytes()
+    for n in (256, 1024, 4096, 16384):
+        if L.attnres_lrid_backward_workspace_bytes(S, n, d, R, H, N.DTYPE_BF16) > cap:
+            break
+    else:
+        pytest.fail("no token count up to 16384 needs more than the static scratch")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    values = [torch.randn(n, d, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(S)]
+    keys = [torch.randn(n, R, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(S)]
+    qdyn = torch.randn(n, R, device="cuda", dtype=torch.bfloat16, generator=g)
+    grad = torch.randn(n, d, device="cuda", dtype=torch.bfloat16, generator=g)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    results = []
+    for noalloc in (False, True):
+        dV = [torch.empty_like(v) for v in values]
+        dK = [torch.empty_like(k) for k in keys]
+        dq = torch.empty_like(qdyn)
+        common = [
+            S, n, d, R, H, N.DTYPE_BF16,
+            N.ptr_array([v.data_ptr() for v in values]), N.i64_array([d] * S),
+            N.ptr_array([k.data_ptr() for k in keys]), N.i64_array([R] * S),
+            N.QUERY_DYNAMIC, None, None, p(qdyn), 0.125, 1, F32_EPS, None, N.NORM_NONE,
+            float(torch.finfo(torch.bfloat16).eps), p(grad), None, None,
+            N.ptr_array([t.data_ptr() for t in dV]), N.ptr_array([t.data_ptr() for t in dK]),
+            p(dq), None, None, None,
+        ]
+        if noalloc:
+            N.check(L.attnres_lrid_backward_noalloc(*common, stream), "attnres_lrid_backward_noalloc")
+        else:
+            N.check(L.attnres_lrid_backward(*common, None, 0, stream), "attnres_lrid_backward")
+        torch.cuda.synchronize()
+        results.append((dV, dK, dq))
+    (dV0, dK0, dq0), (dV1, dK1, dq1) = results
+    for x, y in zip(dV1 + dK1 + [dq1], dV0 + dK0 + [dq0]):
+        assert_close("grad", x.float().cpu().numpy(), y.float().cpu().numpy(), torch.bfloat16)
