@@ -81,22 +81,17 @@ bool values_vectorizable(int S, int esz, const void* const* values, const int64_
   return true;
 }
 
-// Which LRID kernel family to use (ATTNRES_B200_PATH):
-//   auto (default) : the streaming warp pipeline, else the CTA-tile
-//                    bulk-copy pipeline, else register streaming -- the first
-//                    whose layout rules hold
-//   tma            : skip the warp-per-token pipeline
-//   warp           : skip the CTA-tile pipeline
-//   simt           : register-streaming kernels only
-enum PathChoice { PATH_AUTO, PATH_SIMT, PATH_TMA, PATH_WARP };
+// Which LRID kernel to use. The streaming warp pipeline (bulk copies into
+// per-warp rings) serves every layout whose rows are 16-byte aligned and split
+// into 512-byte chunks per head; the register-streaming kernel serves every
+// other layout (unaligned or odd-width rows, odd head counts). Tests set
+// ATTNRES_B200_PATH=simt to run the register-streaming kernel on layouts the
+// streaming pipeline would take.
+enum PathChoice { PATH_AUTO, PATH_SIMT };
 
 PathChoice path_choice() {
   const char* v = getenv("ATTNRES_B200_PATH");
-  if (!v || !*v || !strcmp(v, "auto")) return PATH_AUTO;
-  if (!strcmp(v, "simt")) return PATH_SIMT;
-  if (!strcmp(v, "tma")) return PATH_TMA;
-  if (!strcmp(v, "warp")) return PATH_WARP;
-  return PATH_AUTO;
+  return (v && !strcmp(v, "simt")) ? PATH_SIMT : PATH_AUTO;
 }
 
 // Key rows (and per-token queries) admit 16-byte bulk copies.
@@ -144,9 +139,8 @@ const char* attnres_last_error(void) { return g_last_error.c_str(); }
 int attnres_device_status(unsigned* status, int reset) {
   if (!status) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "status is NULL");
   unsigned s1 = 0, s2 = 0;
-  cudaError_t e = attnres::read_device_status(&s1, reset != 0);
+  cudaError_t e = attnres::read_warp_status(&s2, reset != 0);
   unsigned s3 = 0;
-  if (e == cudaSuccess) e = attnres::read_warp_status(&s2, reset != 0);
   if (e == cudaSuccess) e = attnres::read_keyproj_status(&s3, reset != 0);
   unsigned s4 = 0;
   if (e == cudaSuccess) e = attnres::read_keyproj_bwd_status(&s4, reset != 0);
@@ -187,17 +181,12 @@ int attnres_lrid_forward(int num_sources, int64_t num_tokens, int value_dim, int
   const bool bulk = pc != PATH_SIMT && vec && plan.vec == 16 / esz &&
                     keys_bulk_copyable(num_sources, key_dim, esz, keys, key_row_strides,
                                        has_qd ? query_dynamic : nullptr);
-  attnres::TmaLayout wl{}, tl{};
-  attnres::LridPlan tplan{};
+  attnres::TmaLayout wl{};
   int nw = 0;
-  const bool warp = bulk && pc != PATH_TMA &&
-                    attnres::lrid_warp_plan(plan, esz, false, false, has_qd, output_norm, &wl, &nw);
-  const bool tma = bulk && !warp && pc != PATH_WARP &&
-                   attnres::lrid_tma_plan(plan, esz, false, false, has_qd, &tplan, &tl);
+  const bool warp = bulk && attnres::lrid_warp_plan(plan, esz, false, false, has_qd, output_norm, &wl, &nw);
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
   cudaError_t e = warp ? attnres::lrid_warp_forward_launch(dtype, plan, wl, nw, io, cs)
-                  : tma ? attnres::lrid_tma_forward_launch(dtype, tplan, tl, io, cs)
-                        : attnres::lrid_forward_launch(dtype, plan, io, cs);
+                       : attnres::lrid_forward_launch(dtype, plan, io, cs);
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_forward launch");
   return ATTNRES_OK;
 }
@@ -220,20 +209,14 @@ size_t attnres_lrid_backward_workspace_bytes(int num_sources, int64_t num_tokens
     size_t b = 0;
     if (attnres::lrid_workspace(dtype, plan, &b) != cudaSuccess) return 0;
     if (b > best) best = b;
-    for (int variant = 0; variant < 8 && v == 1; ++variant) {
+    for (int variant = 0; variant < 4 && v == 1; ++variant) {
       attnres::TmaLayout tl{};
-      attnres::LridPlan tplan{};
       const bool y = variant & 1, qd = variant & 2;
-      if (variant & 4) {
-        int nw = 0;
-        if (!attnres::lrid_warp_plan(plan, elem_size(dtype), true, y, qd,
-                                     y ? ATTNRES_NORM_ROW : ATTNRES_NORM_NONE, &tl, &nw))
-          continue;
-        if (attnres::lrid_warp_workspace(dtype, plan, tl, nw, &b) != cudaSuccess) return 0;
-      } else {
-        if (!attnres::lrid_tma_plan(plan, elem_size(dtype), true, y, qd, &tplan, &tl)) continue;
-        if (attnres::lrid_tma_workspace(dtype, tplan, tl, &b) != cudaSuccess) return 0;
-      }
+      int nw = 0;
+      if (!attnres::lrid_warp_plan(plan, elem_size(dtype), true, y, qd, y ? ATTNRES_NORM_ROW : ATTNRES_NORM_NONE,
+                                   &tl, &nw))
+        continue;
+      if (attnres::lrid_warp_workspace(dtype, plan, tl, nw, &b) != cudaSuccess) return 0;
       if (b > best) best = b;
     }
   }
@@ -286,19 +269,14 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
   const bool bulk = pc != PATH_SIMT && vec && plan.vec == 16 / esz &&
                     keys_bulk_copyable(num_sources, key_dim, esz, keys, key_row_strides,
                                        has_qd ? query_dynamic : nullptr);
-  attnres::TmaLayout wl{}, tl{};
-  attnres::LridPlan tplan{};
+  attnres::TmaLayout wl{};
   int nw = 0;
-  const bool warp = bulk && pc != PATH_TMA &&
-                    attnres::lrid_warp_plan(plan, esz, true, has_y, has_qd, output_norm, &wl, &nw);
-  const bool tma = bulk && !warp && pc != PATH_WARP &&
-                   attnres::lrid_tma_plan(plan, esz, true, has_y, has_qd, &tplan, &tl);
+  const bool warp = bulk && attnres::lrid_warp_plan(plan, esz, true, has_y, has_qd, output_norm, &wl, &nw);
   const bool need_ws = query_mode != ATTNRES_QUERY_DYNAMIC || grad_logit_bias != nullptr;
   if (need_ws) {
     size_t need = 0;
     cudaError_t e = warp ? attnres::lrid_warp_workspace(dtype, plan, wl, nw, &need)
-                    : tma ? attnres::lrid_tma_workspace(dtype, tplan, tl, &need)
-                          : attnres::lrid_workspace(dtype, plan, &need);
+                         : attnres::lrid_workspace(dtype, plan, &need);
     if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward workspace query");
     if (!workspace || workspace_bytes < need)
       return fail(ATTNRES_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
@@ -311,8 +289,7 @@ int attnres_lrid_backward(int num_sources, int64_t num_tokens, int value_dim, in
                           grad_query, grad_query_gate, grad_query_dynamic, grad_logit_bias, workspace};
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
   cudaError_t e = warp ? attnres::lrid_warp_backward_launch(dtype, plan, wl, nw, io, gio, cs)
-                  : tma ? attnres::lrid_tma_backward_launch(dtype, tplan, tl, io, gio, cs)
-                        : attnres::lrid_backward_launch(dtype, plan, io, gio, cs);
+                       : attnres::lrid_backward_launch(dtype, plan, io, gio, cs);
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_backward launch");
   return ATTNRES_OK;
 }

@@ -2,7 +2,7 @@
 // streaming one token row at a time through a private bulk-copy ring (the
 // kernel template; instantiated by lrid_stream_*.cu, launched by lrid_warp.cu).
 //
-// Arithmetic and semantics are those of lrid.cu / lrid_tma.cu (fp32, the
+// Arithmetic and semantics are those of lrid.cu (fp32, the
 // reference's _lrid_read_torch_list attnres_ops.py:4195-4232 and the backward
 // of _lrid_attnres_list_backward_kernel attnres_ops.py:602-746). Layout:
 //   * every warp of a persistent CTA owns whole token rows (t = blockIdx.x +

@@ -58,7 +58,7 @@ struct LridGradIO {
   void* workspace;
 };
 
-// Shared-memory pipeline layout of the bulk-copy (TMA) kernels.
+// Shared-memory layout of the streaming (bulk-copy) kernels.
 struct TmaLayout {
   int stages;       // ring depth
   int stage_bytes;  // bytes per stage: keys [S][tpc][R], values [S][tpc][d], g, y, query
@@ -77,15 +77,6 @@ cudaError_t lrid_forward_launch(int dtype, const LridPlan& p, const LridIO& io, 
 cudaError_t lrid_backward_launch(int dtype, const LridPlan& p, const LridIO& io,
                                  const LridGradIO& gio, cudaStream_t st);
 
-// Bulk-copy (TMA) pipelined variant; usable when lrid_tma_layout() succeeds.
-bool lrid_tma_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool has_qd, LridPlan* out,
-                   TmaLayout* L);
-cudaError_t lrid_tma_workspace(int dtype, const LridPlan& p, const TmaLayout& L, size_t* bytes);
-cudaError_t lrid_tma_forward_launch(int dtype, const LridPlan& p, const TmaLayout& L, const LridIO& io,
-                                    cudaStream_t st);
-cudaError_t lrid_tma_backward_launch(int dtype, const LridPlan& p, const TmaLayout& L, const LridIO& io,
-                                     const LridGradIO& gio, cudaStream_t st);
-cudaError_t read_device_status(unsigned* status, bool reset);
 
 // Warp-per-token bulk-copy variant (row widths that split into 32-lane chunks per head).
 bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool has_qd, int out_norm,

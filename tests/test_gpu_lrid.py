@@ -15,12 +15,11 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["auto", "tma", "simt"])
+@pytest.fixture(autouse=True, params=["auto", "simt"])
 def kernel_path(request, monkeypatch):
-    """Run every LRID test on each kernel family: `auto` picks the
-    warp-per-token bulk-copy pipeline where the row widths allow it, `tma` the
-    CTA-tile bulk-copy pipeline, `simt` the register-streaming kernels that
-    serve every layout (each falls back to the next when its rules fail)."""
+    """Run every LRID test on both kernels: `auto` picks the streaming warp
+    pipeline (bulk copies into per-warp rings) where the row layout allows it,
+    `simt` forces the register-streaming kernel that serves every layout."""
     monkeypatch.setenv("ATTNRES_B200_PATH", request.param)
     yield request.param
     if request.param != "simt":
