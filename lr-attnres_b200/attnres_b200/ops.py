@@ -145,7 +145,7 @@ def _lrid_forward_impl(values, keys, query, query_gate, query_dynamic, logit_bia
             N.ptr_array([t.data_ptr() for t in krows]), N.i64_array(kstr),
             qmode, _ptr(q), _ptr(g), _ptr(qd),
             float(logit_scale), int(bool(key_norm)), F32_EPS, _ptr(bias),
-            int(output_norm), float(torch.finfo(dtype).eps),
+            int(output_norm), _rms_eps(),
             _ptr(out), _ptr(out_inv) if output_norm != N.NORM_NONE else None,
             _ptr(alpha) if save_aux else None, _ptr(kinv) if save_aux else None,
             _stream_ptr(device),
@@ -215,7 +215,7 @@ def _lrid_backward_impl(values, keys, query, query_gate, query_dynamic, logit_bi
             N.ptr_array([t.data_ptr() for t in krows]), N.i64_array(kstr),
             qmode, _ptr(q), _ptr(g), _ptr(qd),
             float(logit_scale), int(bool(key_norm)), F32_EPS, _ptr(bias),
-            int(output_norm), float(torch.finfo(dtype).eps),
+            int(output_norm), _rms_eps(),
             _ptr(grad_output), _ptr(y), _ptr(output_inv_rms) if y is not None else None,
             N.ptr_array([t.data_ptr() for t in grad_values]) if write_dv else None,
             N.ptr_array([t.data_ptr() for t in grad_keys]),
@@ -453,7 +453,7 @@ def _base_forward_impl(values, query, logit_bias, key_norm, normalize_output):
     device = values[0].device
     q = query.to(dtype).reshape(d).contiguous()
     bias = None if logit_bias is None else logit_bias.to(torch.float32).reshape(-1).contiguous()
-    eps = float(torch.finfo(dtype).eps)
+    eps = _rms_eps()
     out = torch.empty((*_lead_shape(values[0]), d), device=device, dtype=dtype)
     inv = torch.empty((n,) if normalize_output else (1,), device=device, dtype=torch.float32)
     with torch.cuda.device(device):
@@ -507,7 +507,7 @@ def base_read_backward(
     device = values[0].device
     q = query.to(dtype).reshape(d).contiguous()
     bias = None if logit_bias is None else logit_bias.to(torch.float32).reshape(-1).contiguous()
-    eps = float(torch.finfo(dtype).eps)
+    eps = _rms_eps()
     g = grad_output.to(dtype).reshape(n, d).contiguous()
     y = normed_output.to(dtype).reshape(n, d).contiguous() if normalize_output else None
     inv = output_inv_rms.to(torch.float32).contiguous() if normalize_output else None
@@ -565,6 +565,14 @@ base_read.register_autograd(_base_read_bwd, setup_context=_base_read_setup)
 # ---------------------------------------------------------------------------
 def _norm(x: Tensor) -> Tensor:
     return F.rms_norm(x, (x.size(-1),))
+
+
+def _rms_eps() -> float:
+    """The eps of the reference's RMS norms, F.rms_norm(x, eps=None)
+    (attnres_ops.py:49-52, model.py:28-31): PyTorch takes the eps of the type it
+    computes in, fp32 for fp32, fp16 and bf16 inputs alike -- not the eps of the
+    16-bit input dtype (7.8e-3 for bf16, which would change rows of small RMS)."""
+    return F32_EPS
 
 
 def source_logit_bias(source_counts, source_logit_biases, n_sources: int, device) -> Optional[Tensor]:
@@ -724,7 +732,7 @@ def _kv_project(values, weight, value_norm):
     with torch.cuda.device(device):
         rc = N.load().attnres_lrid_key_projection(
             S, n, d, R, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
-            _ptr(w), int(w.stride(0)), int(bool(value_norm)), float(torch.finfo(dtype).eps),
+            _ptr(w), int(w.stride(0)), int(bool(value_norm)), _rms_eps(),
             _ptr(keys), _ptr(inv), _stream_ptr(device))
     N.check(rc, "attnres_lrid_key_projection")
     return keys, inv
@@ -964,7 +972,7 @@ def phase1_from_logits(values: List[Tensor], logits: Tensor, normalize_output: b
         rc = N.load().attnres_phase1_forward(
             S, Q, n, d, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
             _ptr(lg), _dtype_code(lg.dtype), N.NORM_ROW if normalize_output else N.NORM_NONE,
-            float(torch.finfo(dtype).eps), _ptr(out), _ptr(lse), _ptr(inv) if normalize_output else None,
+            _rms_eps(), _ptr(out), _ptr(lse), _ptr(inv) if normalize_output else None,
             _stream_ptr(device))
     N.check(rc, "attnres_phase1_forward")
     return out, lse, inv
@@ -1001,7 +1009,7 @@ def phase1_from_logits_backward(values: List[Tensor], logits: Tensor, grad_outpu
         rc = N.load().attnres_phase1_backward(
             S, Q, n, d, _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
             _ptr(lg), _dtype_code(lg.dtype), N.NORM_ROW if normalize_output else N.NORM_NONE,
-            float(torch.finfo(dtype).eps), _ptr(g), _ptr(gl), _ptr(y), _ptr(yi),
+            _rms_eps(), _ptr(g), _ptr(gl), _ptr(y), _ptr(yi),
             N.ptr_array([t.data_ptr() for t in gv]), _ptr(dlg), _stream_ptr(device))
     N.check(rc, "attnres_phase1_backward")
     return gv, dlg.reshape(logits.shape)
@@ -1157,7 +1165,7 @@ PHASE2_LRID, PHASE2_BASE, PHASE2_LOGIT = 0, 1, 2
 def _phase2_key_eps(mode, dtype):
     # LRID keys are normed as _norm(partial_key.float()) (attnres_ops.py:4127);
     # the base key as _norm(partial_value) in the value dtype (:2638)
-    return float(torch.finfo(torch.float32 if mode == PHASE2_LRID else dtype).eps)
+    return _rms_eps()
 
 
 @torch.library.custom_op("attnres::phase2", mutates_args=())
@@ -1185,7 +1193,7 @@ def phase2(mode: int, partial_value: Tensor, partial_key: Optional[Tensor], part
         rc = N.load().attnres_phase2_forward(
             int(mode), n, d, R, _dtype_code(dtype), _ptr(pv), _ptr(pk), _ptr(lg), _ptr(q), float(logit_scale),
             int(bool(key_norm)), _phase2_key_eps(mode, dtype), float(logit_bias_value), _ptr(b), _ptr(io), _ptr(lse),
-            int(bool(normalize_output)), float(torch.finfo(dtype).eps), _ptr(out), _ptr(inv),
+            int(bool(normalize_output)), _rms_eps(), _ptr(out), _ptr(inv),
             _stream_ptr(pv.device))
     N.check(rc, "attnres_phase2_forward")
     return out.reshape(partial_value.shape), inv
@@ -1366,7 +1374,7 @@ def lrid_fused_projection(x: Tensor, weight: Tensor, output_dim: int, rank: int,
         inv = torch.empty((n, num_heads), device=x.device, dtype=torch.float32)
         with torch.cuda.device(x.device):
             rc = N.load().attnres_head_rms_norm_forward(n, rank, num_heads, _dtype_code(dt), _ptr(kq), kq.stride(0),
-                                                         float(torch.finfo(dt).eps), _ptr(key), _ptr(inv),
+                                                         _rms_eps(), _ptr(key), _ptr(inv),
                                                          _stream_ptr(x.device))
         N.check(rc, "attnres_head_rms_norm_forward")
     else:

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from cases import CASES, case_inputs
-from gpu_helpers import assert_close, dev_rows, rounded, to_np
+from gpu_helpers import RMS_EPS, assert_close, dev_rows, rounded, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -35,7 +35,7 @@ def run_base(inp, B, T, key_norm, dtype, normalize_output=False, bias=False):
 
 
 def oracle_base(inp, key_norm, dtype, normalize_output, bias):
-    eps = float(torch.finfo(dtype).eps)
+    eps = RMS_EPS
     vals = rounded(inp["values"], dtype)
     q = rounded(inp["query"], dtype)
     b = inp["logit_bias"] if bias else None

@@ -2,34 +2,41 @@
 
 The per-token outputs do not depend on the batch size, but the parameter
 gradients do: dq / d(gate) (config 3) and dW_k / dq (config 4) are fp32 sums
-over every token row, reduced per CTA and then in a fixed order. At these
-sizes (32768 and 131072 tokens) the tests check a size-independent property of
-those sums -- the whole batch equals the fp64 sum of its token shards, each
-run on its own -- and compare out / dV / dK (config 3) and out / dV (config 4)
-on token slices at both ends of the batch against the fp64 oracle.
+over every token row (2.2 million rows x sources for dW_k), reduced per CTA and
+then in a fixed order. At these sizes (32768 and 131072 tokens) they are
+compared with a float64 PyTorch composition of the same read, computed in
+token chunks on the GPU, at the bf16 tolerance (rtol 2e-2, atol 1e-2 of the
+largest entry), and out / dV / dK (config 3) and out / dV (config 4) on token
+slices at both ends of the batch against the fp64 oracle.
 """
 import numpy as np
 import pytest
 import torch
 
-from gpu_helpers import assert_close, to_np
+from gpu_helpers import RMS_EPS, assert_close, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
-# fp32 sums over ~10^5 - 10^6 terms, accumulated per CTA in a different order
-# for the whole batch and for each shard: allow 2e-5 of the largest entry
-SUM_RTOL, SUM_ATOL_REL = 1e-5, 2e-5
+CHUNK = 4096  # tokens per float64 reference chunk (about 1 GB of values at config 4)
 
 
 def _slices(n):
     return (slice(0, 64), slice(n - 64, n))
 
 
-def _assert_additive(name, full, shards):
-    total = sum(shards)
-    torch.testing.assert_close(full, total, rtol=SUM_RTOL, atol=SUM_ATOL_REL * float(full.abs().max()),
-                               msg=lambda m: f"{name}: {m}")
+def _read64(V, K, q, H, scale, gate=None, qd=None):
+    """float64 LRID read of one token chunk: V [S, n, d], K [S, n, R], static
+    query q [H, dk] (+ gate [H] * dynamic query [n, H, dk]); key rms norm with
+    the fp32 eps (F.rms_norm's for 16-bit inputs)."""
+    S, n, d = V.shape
+    dk = K.shape[-1] // H
+    Kh = K.reshape(S, n, H, dk)
+    Kh = Kh * torch.rsqrt(Kh.pow(2).mean(-1, keepdim=True) + RMS_EPS)
+    qq = q.reshape(1, H, dk) + (gate.reshape(1, H, 1) * qd if qd is not None else 0)
+    logits = (Kh * qq.unsqueeze(0)).sum(-1) * scale  # [S, n, H]
+    a = torch.softmax(logits, dim=0)
+    return torch.einsum("snh,snhe->nhe", a, V.reshape(S, n, H, d // H)).reshape(n, d)
 
 
 def test_config3_full_size_gated_read():
@@ -54,9 +61,16 @@ def test_config3_full_size_gated_read():
         return out, r
 
     out, (dV, dK, dq, dgate, dqd, _) = run(slice(0, N))
-    shards = [run(slice(i, i + N // 4))[1] for i in range(0, N, N // 4)]
-    _assert_additive("dq", dq.double(), [r[2].double() for r in shards])
-    _assert_additive("dgate", dgate.double(), [r[3].double() for r in shards])
+    q64 = qs.double().requires_grad_(True)
+    g64 = gate.double().requires_grad_(True)
+    for c in range(0, N, CHUNK):
+        sl = slice(c, c + CHUNK)
+        V = torch.stack([v[0, sl] for v in values]).double()
+        K = torch.stack([k[0, sl] for k in keys]).double()
+        o = _read64(V, K, q64, H, scale, g64, qd[0, sl].double())
+        (o * g[0, sl].double()).sum().backward()
+    assert_close("dq", to_np(dq).reshape(-1), to_np(q64.grad).reshape(-1), bf, sum_terms=N)
+    assert_close("dgate", to_np(dgate).reshape(-1), to_np(g64.grad).reshape(-1), bf, sum_terms=N)
     for sl in _slices(N):
         v = np.stack([to_np(x[0, sl]) for x in values])
         k = np.stack([to_np(x[0, sl]) for x in keys])
@@ -66,7 +80,7 @@ def test_config3_full_size_gated_read():
         assert_close("out", to_np(out[0, sl]), ref_out, bf)
         assert_close("dV", np.stack([to_np(x[0, sl]) for x in dV]), ref["dV"], bf)
         assert_close("dK", np.stack([to_np(x[0, sl]) for x in dK]), ref["dK"], bf)
-        assert_close("dq_dynamic", to_np(dqd.reshape(N, H, R // H)[sl]), ref["dq_dynamic"], bf)
+        assert_close("dq_dynamic", to_np(dqd.reshape(N, R)[sl]), ref["dq_dynamic"], bf)
 
 
 def test_config4_full_size_key_from_value_read():
@@ -90,14 +104,18 @@ def test_config4_full_size_key_from_value_read():
 
     out, r = run(slice(0, N))
     dV, dW, dq = r[0], r[1], r[2]
-    shard_dW, shard_dq = [], []
-    for i in range(0, N, N // 4):
-        rs = run(slice(i, i + N // 4))[1]
-        shard_dW.append(rs[1].double())
-        shard_dq.append(rs[2].double())
-    _assert_additive("dW_k", dW.double(), shard_dW)
-    _assert_additive("dq", dq.double(), shard_dq)
-    eps = float(torch.finfo(bf).eps)
+    w64 = w.double().requires_grad_(True)
+    q64 = q.double().requires_grad_(True)
+    for c in range(0, N, CHUNK):
+        sl = slice(c, c + CHUNK)
+        V = torch.stack([v[0, sl] for v in values]).double()
+        nhat = V * torch.rsqrt(V.pow(2).mean(-1, keepdim=True) + RMS_EPS)
+        o = _read64(V, nhat @ w64.t(), q64, H, scale)
+        (o * g[0, sl].double()).sum().backward()
+        del V, nhat, o
+    assert_close("dW_k", to_np(dW), to_np(w64.grad), bf, sum_terms=N)
+    assert_close("dq", to_np(dq).reshape(-1), to_np(q64.grad).reshape(-1), bf, sum_terms=N)
+    eps = RMS_EPS
     for sl in _slices(N):
         v = np.stack([to_np(x[0, sl]) for x in values])
         kw = dict(query=to_np(q))

@@ -5,6 +5,8 @@ _norm_lrid_key (model.py:33-36), the query columns split off; forward and the
 gradients of x and of the projection weight."""
 import pytest
 import torch
+
+from gpu_helpers import RMS_EPS
 import torch.nn.functional as F
 
 pytestmark = pytest.mark.gpu
@@ -59,11 +61,11 @@ def test_head_rms_norm_reads_a_strided_key_slice():
     y = torch.empty(n, R, device="cuda", dtype=torch.bfloat16)
     inv = torch.empty(n, H, device="cuda")
     rc = N.load().attnres_head_rms_norm_forward(n, R, H, 2, ctypes.c_void_p(kq.data_ptr()), kq.stride(0),
-                                                float(torch.finfo(torch.bfloat16).eps), ctypes.c_void_p(y.data_ptr()),
+                                                RMS_EPS, ctypes.c_void_p(y.data_ptr()),
                                                 ctypes.c_void_p(inv.data_ptr()), None)
     N.check(rc, "head norm")
     torch.cuda.synchronize()
     # against fp32 math (bf16 tolerance), as the other bf16 parity checks
     xk = kq[:, :R].float().reshape(n, H, R // H)
-    want = (xk * torch.rsqrt(xk.pow(2).mean(-1, keepdim=True) + torch.finfo(torch.bfloat16).eps)).reshape(n, R)
+    want = (xk * torch.rsqrt(xk.pow(2).mean(-1, keepdim=True) + RMS_EPS)).reshape(n, R)
     torch.testing.assert_close(y.float(), want, rtol=2e-2, atol=1e-2)

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from cases import CASES, case_inputs
-from gpu_helpers import assert_close, dev_rows, rounded, to_np
+from gpu_helpers import RMS_EPS, assert_close, dev_rows, rounded, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -92,7 +92,7 @@ def oracle_lrid(inp, H, scale, key_norm, query_kind, dtype, norm, bias):
     keys = rounded(inp["keys"], dtype)
     g = rounded(inp["grad_output"], dtype)
     kw = dict(output_norm=norm, logit_bias=inp["logit_bias"] if bias else None,
-              output_eps=float(torch.finfo(dtype).eps))
+              output_eps=RMS_EPS)
     if query_kind == "static":
         kw["query"] = rounded(inp["query"], dtype)
     elif query_kind == "dynamic":
@@ -108,10 +108,13 @@ def oracle_lrid(inp, H, scale, key_norm, query_kind, dtype, norm, bias):
     return grads
 
 
-def compare(res, ref, dtype, n_tokens):
+def compare(res, ref, dtype, n_tokens, out_norm=False):
+    """With the output normalised, the 16-bit backward reads the saved 16-bit
+    normed output (as the reference's fused backward does), so dV / dK carry an
+    error proportional to their own scale: their absolute floor scales too."""
     assert_close("out", res["out"], ref["out"], dtype)
-    assert_close("dV", res["dV"], ref["dV"], dtype)
-    assert_close("dK", res["dK"], ref["dK"], dtype)
+    assert_close("dV", res["dV"], ref["dV"], dtype, scaled_atol=out_norm)
+    assert_close("dK", res["dK"], ref["dK"], dtype, scaled_atol=out_norm)
     for name in ("dq", "dgate", "dq_dynamic", "dbias"):
         if name in ref:
             summed = name in ("dq", "dgate", "dbias") and ref[name].ndim == 1
@@ -172,7 +175,7 @@ def test_lrid_shapes_bf16(name, S, D, R, H, scale, query_kind, norm):
     res = run_lrid(inp, B, T, H, scale, True, query_kind, torch.bfloat16, normalize_output=norm)
     ref = oracle_lrid(inp, H, scale, True, query_kind, torch.bfloat16,
                       (oracle.NORM_PER_HEAD if H == 1 else oracle.NORM_ROW) if norm else oracle.NORM_NONE, False)
-    compare(res, ref, torch.bfloat16, B * T)
+    compare(res, ref, torch.bfloat16, B * T, out_norm=norm)
 
 
 def test_lrid_config3_many_tokens_per_cta():
@@ -424,7 +427,7 @@ def test_lrid_output_norm_read_matches_the_unnormed_read_then_rms_norm(kernel_pa
             out = ops.lrid_attention_residual_read(vs, ks, qq, H, 0.125, True, normalize_output=True)
         else:
             out = ops.lrid_attention_residual_read(vs, ks, qq, H, 0.125, True)
-            out = torch.nn.functional.rms_norm(out.float(), (D,), eps=float(torch.finfo(torch.bfloat16).eps))
+            out = torch.nn.functional.rms_norm(out.float(), (D,), eps=RMS_EPS)
         out.float().backward(g.float())
         grads.append((out.float(), qq.grad.float(), vs[2].grad.float(), ks[6].grad.float()))
     for name, x, y in zip(("out", "dq", "dV2", "dK6"), *grads):

@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from cases import CASES, case_inputs
-from gpu_helpers import assert_close, rounded, to_np
+from gpu_helpers import RMS_EPS, assert_close, rounded, to_np
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -29,7 +29,7 @@ def run_phase1(inp, Q, B, T, dtype, normalize_output, stacked=False):
 
 def oracle_phase1(inp, dtype, normalize_output):
     v, g = rounded(inp["values"], dtype), rounded(inp["grad_output"], dtype)
-    eps = float(torch.finfo(dtype).eps)
+    eps = RMS_EPS
     out, lse, _, _, _ = oracle.phase1_forward(v, inp["logits"], normalize_output, eps)
     res = oracle.phase1_backward(v, inp["logits"], g, inp["grad_lse"], normalize_output, eps)
     res.update(out=out, lse=lse)

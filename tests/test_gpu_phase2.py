@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from cases import CASES, case_inputs
-from gpu_helpers import assert_close, rounded, to_np
+from gpu_helpers import RMS_EPS, assert_close, rounded, to_np
 from oracle import oracle
 from test_oracle_golden import phase2_args
 
@@ -67,8 +67,8 @@ def oracle_phase2(case, inp, dtype, saved_output=None):
         r["query"] = rounded(r["query"], dtype)
     mode, kw = phase2_args(case, r)
     if case["mode"] == "base":
-        kw["key_eps"] = float(torch.finfo(dtype).eps)
-    kw["output_eps"] = float(torch.finfo(dtype).eps)
+        kw["key_eps"] = RMS_EPS
+    kw["output_eps"] = RMS_EPS
     base = (r["partial_value"], r["interblock_output"], r["interblock_lse"])
     out, _ = oracle.phase2_forward(mode, *base, **kw)
     res = oracle.phase2_backward(mode, *base, r["grad_output"], saved_output=saved_output, **kw)

@@ -12,7 +12,7 @@ import ctypes
 import pytest
 import torch
 
-from gpu_helpers import assert_close
+from gpu_helpers import RMS_EPS, assert_close
 from attnres_b200 import _native as N
 
 pytestmark = pytest.mark.gpu
@@ -45,7 +45,7 @@ def _call(noalloc, values, keys, query, grad, bias, H, scale=0.125):
         N.ptr_array([v.data_ptr() for v in values]), N.i64_array([d] * S),
         N.ptr_array([k.data_ptr() for k in keys]), N.i64_array([R] * S),
         N.QUERY_STATIC, p(query), None, None, scale, 1, F32_EPS, p(bias), N.NORM_NONE,
-        float(torch.finfo(values[0].dtype).eps), p(grad), None, None,
+        RMS_EPS, p(grad), None, None,
         N.ptr_array([t.data_ptr() for t in dV]), N.ptr_array([t.data_ptr() for t in dK]),
         p(dq), None, None, p(db),
     ]
@@ -136,7 +136,7 @@ def test_noalloc_accepts_calls_that_use_no_scratch():
             N.ptr_array([v.data_ptr() for v in values]), N.i64_array([d] * S),
             N.ptr_array([k.data_ptr() for k in keys]), N.i64_array([R] * S),
             N.QUERY_DYNAMIC, None, None, p(qdyn), 0.125, 1, F32_EPS, None, N.NORM_NONE,
-            float(torch.finfo(torch.bfloat16).eps), p(grad), None, None,
+            RMS_EPS, p(grad), None, None,
             N.ptr_array([t.data_ptr() for t in dV]), N.ptr_array([t.data_ptr() for t in dK]),
             p(dq), None, None, None,
         ]
