@@ -266,6 +266,27 @@ int attnres_block_summary_backward(int64_t num_elements, int dtype, const void* 
                                    float* grad_scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Block summary with the value norm (attnres_block_value_norm): the block
+ * source is the RMS-normed running sum instead of the scaled one
+ * (model.py:991-992, :1004-1005; replaces F.rms_norm(partial + x)):
+ *   sum = partial + x (partial may be NULL),  source = rms_norm(sum)
+ * over rows of row_width elements, eps = `eps` (F.rms_norm's default is the
+ * fp32 eps for fp32, fp16 and bf16 rows). inv_rms (float, num_rows) receives
+ * each row's inverse rms for the backward; sum may be NULL.
+ */
+int attnres_block_summary_norm_forward(int64_t num_rows, int row_width, int dtype, const void* partial,
+                                       const void* x, float eps, void* sum, void* source, float* inv_rms,
+                                       void* stream);
+/*
+ * Backward of the above: grad_total (the gradient of both partial and x) =
+ * round(round(rms_norm_backward(grad_source)) + grad_sum), from the saved sum
+ * and inv_rms; grad_sum may be NULL.
+ */
+int attnres_block_summary_norm_backward(int64_t num_rows, int row_width, int dtype, const void* grad_source,
+                                        const void* grad_sum, const void* sum, const float* inv_rms,
+                                        void* grad_total, void* stream);
+
+/*
  * Per-head RMS norm of key rows: y[r, h*dk + j] = x[r, h*dk + j] * inv_rms[r, h],
  * inv_rms = rsqrt(mean_j x^2 + eps), dk = width / num_heads, fp32 math, y and
  * grad dense [rows, width]; x may be a strided slice (x_row_stride elements),

@@ -11,11 +11,13 @@ from .ops import (
     attention_residual_block_summary,
     attention_residual_read,
     block_summary,
+    block_summary_norm,
     base_read,
     is_fused_attnres_available,
     lrid_attention_residual_read,
     lrid_attention_residual_read_gated,
     lrid_attention_residual_read_key_from_value,
+    lrid_block_source,
     lrid_fused_projection_forward,
     lrid_kv_read,
     lrid_read,
@@ -28,11 +30,13 @@ __all__ = [
     "attention_residual_block_summary",
     "attention_residual_read",
     "block_summary",
+    "block_summary_norm",
     "base_read",
     "is_fused_attnres_available",
     "lrid_attention_residual_read",
     "lrid_attention_residual_read_gated",
     "lrid_attention_residual_read_key_from_value",
+    "lrid_block_source",
     "lrid_fused_projection_forward",
     "lrid_kv_read",
     "lrid_read",

@@ -40,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "attnres_block_summary_forward",
     "attnres_block_summary_backward_workspace_bytes",
     "attnres_block_summary_backward",
+    "attnres_block_summary_norm_forward",
+    "attnres_block_summary_norm_backward",
     "attnres_head_rms_norm_forward",
     "attnres_head_rms_norm_backward",
     "attnres_phase2_forward",
@@ -127,6 +129,10 @@ def load(path=None):
     L.attnres_block_summary_backward_workspace_bytes.argtypes = [I64]
     L.attnres_block_summary_backward.restype = I
     L.attnres_block_summary_backward.argtypes = [I64, I, P, P, P, P, F, P, P, P, SZ, P]
+    L.attnres_block_summary_norm_forward.restype = I
+    L.attnres_block_summary_norm_forward.argtypes = [I64, I, I, P, P, F, P, P, P, P]
+    L.attnres_block_summary_norm_backward.restype = I
+    L.attnres_block_summary_norm_backward.argtypes = [I64, I, I, P, P, P, P, P, P]
     L.attnres_head_rms_norm_forward.restype = I
     L.attnres_head_rms_norm_forward.argtypes = [I64, I, I, I, P, I64, F, P, P, P]
     L.attnres_head_rms_norm_backward.restype = I

@@ -1138,22 +1138,119 @@ def _block_summary_bwd(ctx, grad_sum, grad_source):
 block_summary.register_autograd(_block_summary_bwd, setup_context=_block_summary_setup)
 
 
+@torch.library.custom_op("attnres::block_summary_norm", mutates_args=())
+def block_summary_norm(partial: Optional[Tensor], x: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """sum = partial + x, source = rms_norm(sum) over the last dim (fp32 eps);
+    returns (sum, source, inverse rms [rows] fp32)."""
+    _require_cuda([partial, x], "block summary inputs")
+    dtype = x.dtype
+    d = x.size(-1)
+    xc = x.contiguous()
+    pc = None if partial is None else partial.to(dtype).contiguous()
+    if pc is not None and pc.shape != xc.shape:
+        raise RuntimeError("attnres_b200: block summary partial and x must have one shape")
+    rows = xc.numel() // d
+    out_sum, src = torch.empty_like(xc), torch.empty_like(xc)
+    inv = torch.empty((rows,), device=x.device, dtype=torch.float32)
+    with torch.cuda.device(x.device):
+        rc = N.load().attnres_block_summary_norm_forward(
+            rows, d, _dtype_code(dtype), _ptr(pc), _ptr(xc), _rms_eps(), _ptr(out_sum), _ptr(src), _ptr(inv),
+            _stream_ptr(x.device))
+    N.check(rc, "attnres_block_summary_norm_forward")
+    return out_sum, src, inv
+
+
+@block_summary_norm.register_fake
+def _(partial, x):
+    return x.new_empty(x.shape), x.new_empty(x.shape), x.new_empty((x.numel() // x.size(-1),), dtype=torch.float32)
+
+
+@torch.library.custom_op("attnres::block_summary_norm_backward", mutates_args=())
+def block_summary_norm_backward(grad_source: Tensor, grad_sum: Optional[Tensor], out_sum: Tensor,
+                                inv_rms: Tensor) -> Tensor:
+    """The gradient of partial and of x."""
+    dtype = out_sum.dtype
+    d = out_sum.size(-1)
+    rows = out_sum.numel() // d
+    gs = grad_source.to(dtype).contiguous()
+    gm = None if grad_sum is None else grad_sum.to(dtype).contiguous()
+    g = torch.empty_like(out_sum)
+    with torch.cuda.device(out_sum.device):
+        rc = N.load().attnres_block_summary_norm_backward(
+            rows, d, _dtype_code(dtype), _ptr(gs), _ptr(gm), _ptr(out_sum), _ptr(inv_rms), _ptr(g),
+            _stream_ptr(out_sum.device))
+    N.check(rc, "attnres_block_summary_norm_backward")
+    return g
+
+
+@block_summary_norm_backward.register_fake
+def _(grad_source, grad_sum, out_sum, inv_rms):
+    return out_sum.new_empty(out_sum.shape)
+
+
+def _block_summary_norm_setup(ctx, inputs, output):
+    partial, _ = inputs
+    out_sum, _, inv = output
+    ctx.has_partial = partial is not None
+    ctx.save_for_backward(out_sum, inv)
+
+
+def _block_summary_norm_bwd(ctx, grad_sum, grad_source, grad_inv):
+    out_sum, inv = ctx.saved_tensors
+    if grad_source is None:
+        g = grad_sum
+    else:
+        g = block_summary_norm_backward(grad_source, grad_sum, out_sum, inv)
+    return (g if ctx.has_partial else None, g)
+
+
+block_summary_norm.register_autograd(_block_summary_norm_bwd, setup_context=_block_summary_norm_setup)
+
+
 def attention_residual_block_summary(partial_block: Optional[Tensor], layer_output: Tensor, count: int = 1,
-                                     alpha=1.0, scale: Optional[Tensor] = None):
+                                     alpha=1.0, scale: Optional[Tensor] = None, value_norm: bool = False):
     """The running block sum and the scaled block source of block Attention
     Residuals in one pass: returns (partial_block + layer_output,
     (partial_block + layer_output) * c). c is the learned `scale` (cast to the
     value dtype, as model.py:978-983 does), else count ** -alpha with alpha a
     float or a tensor (model.py:955-959; a tensor alpha keeps its gradient).
     Replaces the add and the multiply of model.py:2377-2389 / :990-1001; the
-    same call scales key sums (model.py:1011-1016)."""
+    same call scales key sums (model.py:1011-1016). value_norm=True
+    (attnres_block_value_norm) returns rms_norm(sum) as the source instead
+    (model.py:991-992, :1004-1005)."""
     dtype = layer_output.dtype
+    if value_norm:
+        # attnres_block_value_norm: the source is rms_norm(sum) (model.py:991-992)
+        out_sum, src, _ = block_summary_norm(partial_block, layer_output)
+        return out_sum, src
     if scale is not None:
         return block_summary(partial_block, layer_output, scale.to(dtype), 1.0)
     if torch.is_tensor(alpha):
         c = torch.exp(-alpha * alpha.new_tensor(float(count)).log())
         return block_summary(partial_block, layer_output, c.to(dtype), 1.0)
     return block_summary(partial_block, layer_output, None, float(count) ** (-float(alpha)))
+
+
+def lrid_block_source(partial_value: Optional[Tensor], value: Tensor, partial_key: Optional[Tensor],
+                      key: Optional[Tensor], count: int = 1, alpha=1.0, scale: Optional[Tensor] = None,
+                      value_norm: bool = False, key_norm: bool = True, key_from_value: bool = False):
+    """One LRID block step: the running value and key sums (model.py:2377-2389)
+    and the block source the read consumes (_lrid_block_source,
+    model.py:1003-1018). Returns (value_sum, value_source, key_sum, key_source):
+      * value_source = rms_norm(value_sum) with value_norm, else value_sum * c
+        (c = the learned `scale`, else count ** -alpha);
+      * key_source = key_sum * c only when neither the value norm, key_norm nor
+        key_from_value is on (model.py:1015-1018), else key_sum.
+    Key arguments may be None (key-from-value sources have no running key)."""
+    value_sum, value_source = attention_residual_block_summary(partial_value, value, count, alpha, scale,
+                                                               value_norm)
+    if key is None:
+        return value_sum, value_source, None, None
+    if value_norm or key_norm or key_from_value:
+        key_sum = key if partial_key is None else block_summary(partial_key, key, None, 1.0)[1]
+        return value_sum, value_source, key_sum, key_sum
+    key_sum, key_source = attention_residual_block_summary(partial_key, key, count, alpha, scale)
+    return value_sum, value_source, key_sum, key_source
 
 
 # ---------------------------------------------------------------------------

@@ -531,6 +531,33 @@ int attnres_block_summary_backward(int64_t num_elements, int dtype, const void* 
   return ATTNRES_OK;
 }
 
+int attnres_block_summary_norm_forward(int64_t num_rows, int row_width, int dtype, const void* partial,
+                                       const void* x, float eps, void* sum, void* source, float* inv_rms,
+                                       void* stream) {
+  if (num_rows < 0 || row_width < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary norm: bad shape");
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (num_rows > 0 && (!x || !source || !inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary norm: NULL x/source/inv_rms");
+  cudaError_t e = attnres::summary_norm_launch(false, num_rows, row_width, dtype, partial, x, eps, sum, source,
+                                               inv_rms, nullptr, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_block_summary_norm_forward launch");
+  return ATTNRES_OK;
+}
+
+int attnres_block_summary_norm_backward(int64_t num_rows, int row_width, int dtype, const void* grad_source,
+                                        const void* grad_sum, const void* sum, const float* inv_rms,
+                                        void* grad_total, void* stream) {
+  if (num_rows < 0 || row_width < 1) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary norm: bad shape");
+  if (elem_size(dtype) == 0) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (num_rows > 0 && (!grad_source || !sum || !inv_rms || !grad_total))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "block summary norm backward: NULL buffer");
+  cudaError_t e = attnres::summary_norm_launch(true, num_rows, row_width, dtype, nullptr, nullptr, 0.f,
+                                               const_cast<void*>(sum), nullptr, const_cast<float*>(inv_rms),
+                                               grad_source, grad_sum, grad_total, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_block_summary_norm_backward launch");
+  return ATTNRES_OK;
+}
+
 static int check_phase2(int mode, int64_t N, int d, int R, int dtype, const void* v, const void* key,
                         const float* logit, const void* q, const void* prev, const float* lse) {
   if (mode < ATTNRES_PHASE2_LRID || mode > ATTNRES_PHASE2_LOGIT)

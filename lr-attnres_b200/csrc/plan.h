@@ -175,6 +175,11 @@ cudaError_t headnorm_launch(bool bwd, int dtype, long long rows, int width, int 
 
 // Block summary (summary.cu).
 int summary_bwd_grid(long long n);
+// Block summary with the value norm: forward (bwd false) sum / source / inv,
+// backward (bwd true) g_total from g_source, g_sum and the saved sum and inv.
+cudaError_t summary_norm_launch(bool bwd, long long rows, int d, int dtype, const void* partial, const void* x,
+                                float eps, void* sum, void* source, float* inv, const void* g_source,
+                                const void* g_sum, void* g_total, cudaStream_t st);
 cudaError_t summary_forward_launch(long long n, int dtype, const void* partial, const void* x,
                                    const float* scale_dev, float scale, void* sum, void* source,
                                    cudaStream_t st);

@@ -158,6 +158,138 @@ __global__ void __launch_bounds__(256) summary_bwd_kernel(const __grid_constant_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Block summary with the value norm (attnres_block_value_norm,
+// model.py:991-992 and :1004-1005): sum = round(partial + x), source =
+// round(rms_norm(sum)) over each row of `d` elements (fp32 eps, as
+// F.rms_norm takes for 16-bit inputs). One warp per row; the inverse rms is
+// saved for the backward.
+// Backward: d_sum_total = round(round(inv * (g - s_hat * mean(g . s_hat))) + g_sum)
+// with s_hat = sum * inv -- the gradient of partial and of x.
+// ---------------------------------------------------------------------------
+struct SummaryNormArgs {
+  const void* partial;  // nullable
+  const void* x;
+  void* sum;  // nullable
+  void* source;
+  float* inv;  // [rows]
+  const void* g_source;
+  const void* g_sum;  // nullable
+  void* g_total;
+  long long rows;
+  int d;
+  float eps;
+};
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) summary_norm_fwd_kernel(const __grid_constant__ SummaryNormArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= a.rows) return;
+  const int np = a.d / VEC;
+  const T* x = static_cast<const T*>(a.x) + row * a.d;
+  const T* p = a.partial ? static_cast<const T*>(a.partial) + row * a.d : nullptr;
+  T* sm = a.sum ? static_cast<T*>(a.sum) + row * a.d : nullptr;
+  T* src = static_cast<T*>(a.source) + row * a.d;
+  float ss = 0.f;
+  for (int i = lane; i < np; i += 32) {
+    const Pack<T, VEC> xv = load_pack<T, VEC>(x + i * VEC);
+    Pack<T, VEC> pv;
+    if (p) pv = load_pack<T, VEC>(p + i * VEC);
+    Pack<T, VEC> yv;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      yv.e[e] = Elem<T>::from_f(Elem<T>::to_f(xv.e[e]) + (p ? Elem<T>::to_f(pv.e[e]) : 0.f));
+      const float y = Elem<T>::to_f(yv.e[e]);
+      ss = fmaf(y, y, ss);
+    }
+    if (sm) *reinterpret_cast<Pack<T, VEC>*>(sm + i * VEC) = yv;
+  }
+  const float inv = rsqrtf(warp_sum(ss) / a.d + a.eps);
+  if (lane == 0) a.inv[row] = inv;
+  // second pass over the row (L1 / L2 resident) for the normalised source
+  for (int i = lane; i < np; i += 32) {
+    const Pack<T, VEC> xv = load_pack<T, VEC>(x + i * VEC);
+    Pack<T, VEC> pv;
+    if (p) pv = load_pack<T, VEC>(p + i * VEC);
+    float o[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float y = Elem<T>::to_f(Elem<T>::from_f(Elem<T>::to_f(xv.e[e]) + (p ? Elem<T>::to_f(pv.e[e]) : 0.f)));
+      o[e] = y * inv;
+    }
+    store_pack<T, VEC>(src + i * VEC, o);
+  }
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) summary_norm_bwd_kernel(const __grid_constant__ SummaryNormArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= a.rows) return;
+  const int np = a.d / VEC;
+  const T* g = static_cast<const T*>(a.g_source) + row * a.d;
+  const T* gm = a.g_sum ? static_cast<const T*>(a.g_sum) + row * a.d : nullptr;
+  const T* y = static_cast<const T*>(a.sum) + row * a.d;
+  T* gt = static_cast<T*>(a.g_total) + row * a.d;
+  const float inv = a.inv[row];
+  float gy = 0.f;
+  for (int i = lane; i < np; i += 32) {
+    const Pack<T, VEC> gv = load_pack<T, VEC>(g + i * VEC);
+    const Pack<T, VEC> yv = load_pack<T, VEC>(y + i * VEC);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) gy = fmaf(Elem<T>::to_f(gv.e[e]), Elem<T>::to_f(yv.e[e]) * inv, gy);
+  }
+  const float m = warp_sum(gy) / a.d;
+  for (int i = lane; i < np; i += 32) {
+    const Pack<T, VEC> gv = load_pack<T, VEC>(g + i * VEC);
+    const Pack<T, VEC> yv = load_pack<T, VEC>(y + i * VEC);
+    Pack<T, VEC> mv;
+    if (gm) mv = load_pack<T, VEC>(gm + i * VEC);
+    float o[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float sh = Elem<T>::to_f(yv.e[e]) * inv;
+      float dx = Elem<T>::to_f(Elem<T>::from_f(inv * (Elem<T>::to_f(gv.e[e]) - sh * m)));
+      if (gm) dx += Elem<T>::to_f(mv.e[e]);
+      o[e] = dx;
+    }
+    store_pack<T, VEC>(gt + i * VEC, o);
+  }
+}
+
+template <typename T>
+static cudaError_t summary_norm_t(bool bwd, const SummaryNormArgs& a, bool vec, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const unsigned grid = static_cast<unsigned>((a.rows * 32 + 255) / 256);
+  if (vec) {
+    if (bwd) summary_norm_bwd_kernel<T, V><<<grid, 256, 0, st>>>(a);
+    else summary_norm_fwd_kernel<T, V><<<grid, 256, 0, st>>>(a);
+  } else {
+    if (bwd) summary_norm_bwd_kernel<T, 1><<<grid, 256, 0, st>>>(a);
+    else summary_norm_fwd_kernel<T, 1><<<grid, 256, 0, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+static bool al16n(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaError_t summary_norm_launch(bool bwd, long long rows, int d, int dtype, const void* partial, const void* x,
+                                float eps, void* sum, void* source, float* inv, const void* g_source,
+                                const void* g_sum, void* g_total, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  SummaryNormArgs a{partial, x, sum, source, inv, g_source, g_sum, g_total, rows, d, eps};
+  const int esz = dtype == ATTNRES_DTYPE_F32 ? 4 : 2;
+  const void* ptrs[] = {partial, x, sum, source, g_source, g_sum, g_total};
+  bool vec = (static_cast<long long>(d) * esz) % 16 == 0;
+  for (const void* q : ptrs) vec = vec && (q == nullptr || al16n(q));
+  switch (dtype) {
+    case ATTNRES_DTYPE_F32: return summary_norm_t<float>(bwd, a, vec, st);
+    case ATTNRES_DTYPE_F16: return summary_norm_t<__half>(bwd, a, vec, st);
+    default: return summary_norm_t<__nv_bfloat16>(bwd, a, vec, st);
+  }
+}
+
 static int summary_grid(long long n, int vec) {
   int dev = 0, nsm = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);

@@ -97,3 +97,55 @@ def test_block_summary_cpu_tensors_fail_loudly():
 
     with pytest.raises(RuntimeError, match="CUDA"):
         A.attention_residual_block_summary(None, torch.randn(4, 8), count=2)
+
+
+def _golden():
+    import json
+    import os
+
+    import numpy as np
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "block_summary.npz")
+    d = np.load(path)
+    return d, json.loads(bytes(d["meta"]).decode())
+
+
+_D, _META = _golden()
+
+
+@pytest.mark.parametrize("case", sorted(_META))
+def test_lrid_block_source_matches_the_reference_model(case):
+    """attnres_b200.lrid_block_source against the reference model's own
+    _lrid_block_source on the running sums (fixtures written by
+    tests/golden/make_block_summary.py): count / sqrt / learned alpha / learned
+    scale, the value norm, and key scaling when key norm is off."""
+    import attnres_b200 as A
+    from gpu_helpers import assert_close
+
+    m = _META[case]
+    dtype = getattr(torch, m["dtype"])
+    get = lambda k: torch.tensor(_D[f"{case}/{k}"], device="cuda")  # noqa: E731
+    t = {k: get(k).to(dtype).requires_grad_(not k.startswith("g")) for k in
+         ("pv", "x", "pk", "k", "g_vsum", "g_vsrc", "g_ksum", "g_ksrc")}
+    alpha = m["alpha"] if m["alpha"] is not None else 1.0
+    scale = None
+    if m["alpha_learned"]:
+        alpha = torch.tensor(m["alpha"], device="cuda", requires_grad=True)
+    if m["scale"] is not None:
+        scale = torch.tensor(m["scale"], device="cuda", requires_grad=True)
+    vsum, vsrc, ksum, ksrc = A.lrid_block_source(t["pv"], t["x"], t["pk"], t["k"], count=m["count"], alpha=alpha,
+                                                 scale=scale, value_norm=m["value_norm"], key_norm=m["key_norm"])
+    for name, got in (("vsum", vsum), ("vsrc", vsrc), ("ksum", ksum), ("ksrc", ksrc)):
+        assert_close(name, got.detach().float().cpu().numpy(), _D[f"{case}/{name}"], dtype)
+    loss = ((vsum * t["g_vsum"]).sum() + (vsrc * t["g_vsrc"]).sum() + (ksum * t["g_ksum"]).sum()
+            + (ksrc * t["g_ksrc"]).sum())
+    loss.float().backward()
+    for name in ("pv", "x", "pk", "k"):
+        assert_close(f"d_{name}", t[name].grad.float().cpu().numpy(), _D[f"{case}/d_{name}"], dtype)
+    n = t["x"].numel()
+    if m["alpha_learned"]:
+        assert_close("d_alpha", alpha.grad.reshape(1).cpu().numpy(), _D[f"{case}/d_alpha"], torch.float32,
+                     sum_terms=n)
+    if scale is not None:
+        assert_close("d_scale", scale.grad.reshape(1).cpu().numpy(), _D[f"{case}/d_scale"], torch.float32,
+                     sum_terms=n)
