@@ -41,6 +41,9 @@ CONFIGS = {
     "config4": dict(S=17, B=32, T=4096, D=2048, R=64, H=1, scale=1 / 8, query="static", kv=True),
     # small case for ncu captures (inputs still > L2)
     "small": dict(S=9, B=4, T=2048, D=1024, R=64, H=1, scale=1 / 8, query="static"),
+    # the whole block LR-AttnRes GPT (attnres_b200.gpt), DDP training step
+    "config5": dict(gpt=True, S=13, B=8, T=2048, D=1024, R=64, H=2, n_layer=24, n_head=16, vocab=100277,
+                    blocks=12, scale=1 / 32 ** 0.5, query="static"),
     # config-4 shapes at 8192 tokens for ncu captures of the key-from-value kernels (570 MB of values)
     "small_kv": dict(S=17, B=2, T=4096, D=2048, R=64, H=1, scale=1 / 8, query="static", kv=True),
 }
@@ -395,6 +398,8 @@ def main():
     c = CONFIGS[args.config]
     if args.impl == "reference":
         return run_reference(args, c)
+    if c.get("gpt"):
+        return run_gpt(args, c)
 
     import torch
     import torch.distributed as dist
@@ -683,6 +688,130 @@ def block_summary_and_phase2(c, stream, torch, device, hbm):
     del xs, ps, pk, o2
     torch.cuda.empty_cache()
     return aux
+
+
+def run_gpt(args, c):
+    """DDP training steps of the block LR-AttnRes GPT
+    (attnres_b200.gpt: 24 layers, d=1024, 16 attention heads, SwiGLU 4x,
+    blocks of 4 sublayers, rank 64, 2 depth heads, vocab 100277), bf16, batch 8
+    x 2048 per GPU, token ids uniform from a seed. A step is forward, cross
+    entropy, backward (DDP all-reduce) and a fused AdamW step. The fused arm
+    uses this package's reads, block summaries and fused projections; the same
+    model with the reference's PyTorch read path is timed beside it."""
+    import torch
+    import torch.distributed as dist
+    from torch.nn.parallel import DistributedDataParallel as DDP
+
+    from attnres_b200.gpt import GPT, GPTConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    steps = args.steps if args.steps != 2000 else 10
+    warmup = args.warmup if args.warmup != 20 else 3
+    B, T = c["B"], c["T"]
+    gen = torch.Generator(device=device).manual_seed(77 + rank)
+    idx = torch.randint(0, c["vocab"], (B, T + 1), device=device, generator=gen)
+    x, y = idx[:, :-1].contiguous(), idx[:, 1:].contiguous()
+
+    def arm(fused):
+        torch.manual_seed(1234)
+        cfg = GPTConfig(n_layer=c["n_layer"], n_head=c["n_head"], n_embd=c["D"], vocab_size=c["vocab"], block_size=T,
+                        attnres_num_blocks=c["blocks"], lrid_rank=c["R"], lrid_num_heads=c["H"],
+                        attn_res_query_init="normal", fused=fused)
+        model = GPT(cfg).to(device).to(torch.bfloat16)
+        nparams = sum(p.numel() for p in model.parameters())
+        net = DDP(model, device_ids=[local], gradient_as_bucket_view=True) if world > 1 else model
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+
+        def step():
+            logits = net(x)
+            loss = F_ce(logits.float().view(-1, logits.size(-1)), y.view(-1))
+            loss.backward()
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+            return loss
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        launches = count_own_launches(step) if fused else 0
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            loss = step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del net, opt, model
+        torch.cuda.empty_cache()
+        return float(t.item()), nparams, launches, float(loss.item())
+
+    import torch.nn.functional as Fn
+
+    F_ce = Fn.cross_entropy
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms, nparams, launches, loss = arm(True)
+    clocks = sampler.stop()
+    ms_torch, _, _, _ = arm(False)
+    tokens = B * T
+    value = tokens * world / (ms * 1e-3)
+    # 6 x params x tokens (dense GEMMs fwd + bwd) + causal attention 6 x L x T x d per token
+    flops = 6.0 * nparams * tokens + 6.0 * c["n_layer"] * T * c["D"] * tokens
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    tpeak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic token ids uniform in [0, 100277) from a seed; random-init weights",
+            "config": {"workload": "config5: block LR-AttnRes GPT training step (fwd + CE + bwd + AdamW), 24 layers, "
+                                   "d=1024, 16 heads, SwiGLU 4x, 12 blocks of 4 sublayers, rank 64, 2 depth heads, "
+                                   "vocab 100277, bf16", "tokens_per_gpu": tokens, "global_tokens": tokens * world,
+                       "parallelism": f"DDP x{world}", "params": nparams,
+                       "l2": "inputs larger than L2 (no flush)"},
+            "roofline": {"kernel": "whole step (cuBLAS GEMMs dominate)", "bound": "tensor",
+                         "achieved": flops / (ms * 1e-3) / 1e12, "peak": tpeak, "unit": "TFLOP/s",
+                         "frac": flops / (ms * 1e-3) / 1e12 / tpeak,
+                         "peak_source": "measured MEASURED_PEAKS.json bf16_tflops_sustained", "traffic": None},
+            "torch_read_path": {"value": tokens * world / (ms_torch * 1e-3), "ms_per_step": ms_torch,
+                                "what": "same model and step with the reference's PyTorch read path"},
+            "gpu_launches": launches * steps, "clocks": clocks, "final_loss": loss, "cpu_baseline": None, "e2e": None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def count_own_launches(step):
+    """Kernels of libattnres_b200 launched by one step (untimed, profiled)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    n = 0
+    for ev in prof.events():
+        if ev.device_type.name == "CUDA" and "attnres::" in ev.name:  # every kernel of the library
+            n += 1
+    return n
 
 
 def run_e2e(args, c, x, device, torch, dist, world):
