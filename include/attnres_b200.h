@@ -216,6 +216,31 @@ int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, in
                                          int value_norm, void* stream);
 
 /*
+ * Key-from-value LRID read, forward, in one kernel (replaces the reference's
+ * LRIDFusedProjection.project_key_from_value, model.py:344-356, followed by
+ * lrid_attention_residual_read, attnres_ops.py:4852): per source
+ *   keys_s = rms_norm(V_s) @ weight^T  (value_norm; eps = value_eps)
+ * rounded to the value dtype, then the LRID read with per-head key norm,
+ * static query [num_heads, key_dim / num_heads], logit_scale, optional
+ * logit_bias [S] and no output norm. Writes output [N, value_dim], keys
+ * [S][N][key_dim] (dtype), value_inv_rms [S][N] (may be NULL without
+ * value_norm) and alpha_out [N][num_heads][S] (float, may be NULL) -- what
+ * attnres_lrid_backward (grad_values = NULL) and
+ * attnres_lrid_key_projection_backward_tc need. f16/bf16, key_dim 64, 2..32
+ * sources, value_dim and value_dim / num_heads multiples of 64, num_heads a
+ * power of two <= 8, 16-byte aligned rows; other shapes return
+ * ATTNRES_ERR_UNSUPPORTED (use attnres_lrid_key_projection +
+ * attnres_lrid_forward).
+ */
+int attnres_lrid_key_from_value_forward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                        int num_heads, int dtype, const void* const* values,
+                                        const int64_t* value_row_strides, const void* weight,
+                                        int64_t weight_row_stride, int value_norm, float value_eps,
+                                        const void* query, float logit_scale, int key_norm, float key_eps,
+                                        const float* logit_bias, void* output, void* keys, float* value_inv_rms,
+                                        float* alpha_out, void* stream);
+
+/*
  * Fused backward of the key projection on the tensor cores, for the one-pass
  * key-from-value read backward (the read ran with grad_values == NULL):
  *   dKs = inv * dK,  coef = inv * <dKs, key> / d

@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "attnres_lrid_backward_noalloc",
     "attnres_lrid_key_projection",
     "attnres_lrid_key_projection_backward",
+    "attnres_lrid_key_from_value_forward",
     "attnres_lrid_key_projection_backward_tc_workspace_bytes",
     "attnres_lrid_key_projection_backward_tc",
     "attnres_block_summary_forward",
@@ -113,6 +114,13 @@ def load(path=None):
     L.attnres_lrid_key_projection.argtypes = [I, I64, I, I, I, PP, PI64, P, I64, I, F, P, P, P]
     L.attnres_lrid_key_projection_backward.restype = I
     L.attnres_lrid_key_projection_backward.argtypes = [I, I64, I, I, I, I, PP, PI64, PP, P, P, P, P, P, P, I, P]
+    L.attnres_lrid_key_from_value_forward.restype = I
+    L.attnres_lrid_key_from_value_forward.argtypes = [
+        I, I64, I, I, I, I,          # S, N, d, R, H, dtype
+        PP, PI64, P, I64,            # values, strides, weight, weight row stride
+        I, F, P, F, I, F, P,         # value_norm, value_eps, query, scale, key_norm, key_eps, logit_bias
+        P, P, P, P, P,               # output, keys, value_inv_rms, alpha, stream
+    ]
     L.attnres_lrid_key_projection_backward_tc_workspace_bytes.restype = SZ
     L.attnres_lrid_key_projection_backward_tc_workspace_bytes.argtypes = [I, I64, I, I, I, I]
     L.attnres_lrid_key_projection_backward_tc.restype = I

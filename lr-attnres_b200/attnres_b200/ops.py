@@ -738,6 +738,44 @@ def _kv_project(values, weight, value_norm):
     return keys, inv
 
 
+def _kv_fused_forward(values, weight, query, bias, H, scale, key_norm, value_norm):
+    """The one-kernel key-from-value forward (projection + read, V streamed
+    through shared memory twice per 8-token tile with the second pass served
+    from L2); returns (out, keys [S, *lead, R], value_inv_rms [S, N],
+    alpha [N, H, S]), or None when it is not selected or the shapes are outside
+    the kernel. It is selected with ATTNRES_KV_FWD=one: at config 4 it measures
+    6.9-8.0 ms against 3.4 ms for the projection kernel followed by the read
+    kernel (its consumers are latency-bound), so the two-kernel path is the
+    default."""
+    if os.environ.get("ATTNRES_KV_FWD", "") != "one":
+        return None
+    S, d, R = len(values), values[0].size(-1), weight.size(0)
+    dtype = values[0].dtype
+    if dtype not in (torch.float16, torch.bfloat16):
+        return None
+    rows, strides = _sources(values, d, dtype)
+    n = _ntok(values[0])
+    device = values[0].device
+    w = weight.to(dtype)
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    q = query.to(dtype).reshape(-1).contiguous()
+    b = None if bias is None else bias.to(torch.float32).reshape(-1).contiguous()
+    out = torch.empty((*_lead_shape(values[0]), d), device=device, dtype=dtype)
+    keys = torch.empty((S, *_lead_shape(values[0]), R), device=device, dtype=dtype)
+    inv = torch.empty((S, n), device=device, dtype=torch.float32)
+    alpha = torch.empty((n, H, S), device=device, dtype=torch.float32)
+    with torch.cuda.device(device):
+        rc = N.load().attnres_lrid_key_from_value_forward(
+            S, n, d, R, int(H), _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            _ptr(w), int(w.stride(0)), int(bool(value_norm)), _rms_eps(), _ptr(q), float(scale), int(bool(key_norm)),
+            F32_EPS, _ptr(b), _ptr(out), _ptr(keys), _ptr(inv), _ptr(alpha), _stream_ptr(device))
+    if rc == 2:  # ATTNRES_ERR_UNSUPPORTED: outside the one-kernel shapes
+        return None
+    N.check(rc, "attnres_lrid_key_from_value_forward")
+    return out, keys, inv, alpha
+
+
 @torch.library.custom_op("attnres::lrid_kv_read", mutates_args=())
 def lrid_kv_read(
     values: List[Tensor],
@@ -756,6 +794,13 @@ def lrid_kv_read(
     alpha [N, H, S] -- the softmax weights, kept so the backward forms dV in
     one pass; [1] when the output is normalised)."""
     values = list(values)
+    if int(output_norm) == N.NORM_NONE and query is not None and query_dynamic is None and len(values) > 1:
+        _require_cuda([*values, key_weight, query, logit_bias], "key-from-value read inputs")
+        fused = _kv_fused_forward(values, key_weight, query, logit_bias, int(num_heads), logit_scale, key_norm,
+                                  value_norm)
+        if fused is not None:
+            out, keys, inv, alpha = fused
+            return out, out.new_empty((1,), dtype=torch.float32), keys, inv, alpha
     keys, inv = _kv_project(values, key_weight, value_norm)
     save = int(output_norm) == N.NORM_NONE
     out, oinv, alpha, _ = _lrid_forward_impl(values, list(keys.unbind(0)), query, query_gate, query_dynamic,

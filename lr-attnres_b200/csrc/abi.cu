@@ -145,6 +145,8 @@ int attnres_device_status(unsigned* status, int reset) {
   unsigned s4 = 0;
   if (e == cudaSuccess) e = attnres::read_keyproj_bwd_status(&s4, reset != 0);
   s3 |= s4;
+  if (e == cudaSuccess) e = attnres::read_kvfused_status(&s4, reset != 0);
+  s3 |= s4;
   if (e != cudaSuccess) return cuda_fail(e, "attnres_device_status");
   *status = s1 | s2 | s3;
   return ATTNRES_OK;
@@ -446,6 +448,33 @@ int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, in
                                                       grad_normed, grad_keys, keys, inv_rms, grad_output,
                                                       alpha, value_norm, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_projection_backward launch");
+  return ATTNRES_OK;
+}
+
+int attnres_lrid_key_from_value_forward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                        int num_heads, int dtype, const void* const* values,
+                                        const int64_t* value_row_strides, const void* weight,
+                                        int64_t weight_row_stride, int value_norm, float value_eps,
+                                        const void* query, float logit_scale, int key_norm, float key_eps,
+                                        const float* logit_bias, void* output, void* keys, float* value_inv_rms,
+                                        float* alpha_out, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values, value_row_strides,
+                         nullptr, nullptr, false);
+  if (rc) return rc;
+  if (num_tokens == 0) return ATTNRES_OK;
+  if (!weight || !query || !output || !keys || (value_norm && !value_inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "key-from-value forward: NULL weight/query/output/keys/inv_rms");
+  const char* why = "";
+  if (!attnres::kvfused_eligible(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values,
+                                 value_row_strides, weight, weight_row_stride, &why))
+    return fail(ATTNRES_ERR_UNSUPPORTED, "key-from-value forward: %s", why);
+  if (!aligned16(output) || !aligned16(keys))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "key-from-value forward: output and keys must be 16-byte aligned");
+  cudaError_t e = attnres::kvfused_forward_launch(
+      num_sources, num_tokens, value_dim, num_heads, dtype, values, value_row_strides, weight, weight_row_stride,
+      value_norm, value_eps, query, logit_scale, key_norm, key_eps, logit_bias, output, keys, value_inv_rms,
+      alpha_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_from_value_forward launch");
   return ATTNRES_OK;
 }
 

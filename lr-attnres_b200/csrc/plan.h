@@ -159,6 +159,18 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
                                   float* grad_weight, void* workspace, size_t workspace_bytes, cudaStream_t st);
 cudaError_t read_keyproj_bwd_status(unsigned* status, bool reset);
 
+// Key-from-value read forward in one kernel (kvfused.cu): projection, key
+// norm, softmax and weighted sum; saves keys [S][N][64], value inverse rms
+// [S][N] and alpha [N][H][S] for the backward.
+bool kvfused_eligible(int S, long long N, int d, int R, int H, int dtype, const void* const* values,
+                      const int64_t* vstr, const void* w, long long w_stride, const char** why);
+cudaError_t kvfused_forward_launch(int S, long long N, int d, int H, int dtype, const void* const* values,
+                                   const int64_t* vstr, const void* w, long long w_stride, int value_norm,
+                                   float value_eps, const void* q, float scale, int key_norm, float key_eps,
+                                   const float* bias, void* out, void* keys, float* vinv, float* alpha,
+                                   cudaStream_t st);
+cudaError_t read_kvfused_status(unsigned* status, bool reset);
+
 // Cached-logit phase 2 (phase2.cu).
 size_t phase2_workspace(int mode, long long N, int d, int R);
 cudaError_t phase2_run(bool bwd, int mode, long long N, int d, int R, int dtype, const void* v, const void* key,

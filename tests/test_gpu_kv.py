@@ -161,3 +161,36 @@ def test_kv_fused_projection_backward_is_deterministic():
         grads.append((ww.grad.clone(), vs[2].grad.clone()))
     for a, b in zip(*grads):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("S,N,D,H,bias,dtype", [
+    (17, 1000, 2048, 1, False, torch.bfloat16),   # config-4 rows
+    (32, 77, 512, 4, False, torch.bfloat16),      # two full 16-source groups, ragged tile
+    (3, 301, 256, 2, True, torch.float16),        # logit biases, ragged last tile
+])
+def test_kv_one_kernel_forward_matches_two_pass(kernel_path, monkeypatch, S, N, D, H, bias, dtype):
+    """The one-kernel key-from-value forward (projection, softmax and weighted
+    sum in one pass of the tile) against the projection kernel followed by the
+    read kernel: out, the saved keys, value inverse rms and softmax weights."""
+    if kernel_path != "auto":
+        pytest.skip("one kernel path is enough")
+    ops = torch.ops.attnres
+    import attnres_b200  # noqa: F401
+
+    torch.manual_seed(S + N)
+    values = [torch.randn(1, N, D, device="cuda", dtype=dtype) for _ in range(S)]
+    w = (torch.randn(64, D, device="cuda") / D ** 0.5).to(dtype)
+    q = (torch.randn(H, 64 // H, device="cuda") * 0.5).to(dtype)
+    b = torch.randn(S, device="cuda") if bias else None
+    res = {}
+    for mode in ("one", "twopass"):  # ATTNRES_KV_FWD: the one-kernel forward, or the default
+        monkeypatch.setenv("ATTNRES_KV_FWD", mode)
+        out, _, keys, inv, alpha = ops.lrid_kv_read(values, w, q, None, None, b, H, 0.25, True, 0, True)
+        torch.cuda.synchronize()
+        res[mode] = (out, keys, inv, alpha)
+    (o1, k1, i1, a1), (o2, k2, i2, a2) = res["one"], res["twopass"]
+    assert_close("out", to_np(o1), to_np(o2), dtype)
+    assert_close("keys", to_np(k1), to_np(k2), dtype)
+    torch.testing.assert_close(i1, i2, rtol=1e-5, atol=0)
+    # a key one bf16 ulp apart (fp32 sums in another order) moves its weights by ~1e-4
+    torch.testing.assert_close(a1, a2, rtol=1e-3, atol=1e-5)
