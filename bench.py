@@ -39,6 +39,9 @@ CONFIGS = {
     "config3": dict(S=13, B=16, T=2048, D=2048, R=64, H=4, scale=1 / 4, query="gated"),
     # keys projected from the values in-op (rms_norm(V) @ W_k^T, tcgen05)
     "config4": dict(S=17, B=32, T=4096, D=2048, R=64, H=1, scale=1 / 8, query="static", kv=True),
+    # config 2 as model.py calls it by default: output RMS norm per head and count-prior logit biases
+    "config2_norm": dict(S=9, B=8, T=2048, D=1024, R=64, H=1, scale=1 / 8, query="static", out_norm=1, bias=True),
+    "small_norm": dict(S=9, B=4, T=2048, D=1024, R=64, H=1, scale=1 / 8, query="static", out_norm=1, bias=True),
     # small case for ncu captures (inputs still > L2)
     "small": dict(S=9, B=4, T=2048, D=1024, R=64, H=1, scale=1 / 8, query="static"),
     # the whole block LR-AttnRes GPT (attnres_b200.gpt), DDP training step
@@ -73,6 +76,9 @@ def algorithmic_bytes(c, esz=2):
     q_tok = R * esz if c["query"] != "static" else 0
     fwd = S * (D + R) * esz + q_tok + D * esz
     bwd = D * esz + S * (D + R) * esz + q_tok + S * (D + R) * esz + q_tok
+    if c.get("out_norm"):
+        # the inverse rms out (fwd) and in (bwd), the normed output read by the backward
+        fwd, bwd = fwd + 4 * c["H"], bwd + D * esz + 4 * c["H"]
     return fwd, bwd
 
 
@@ -273,11 +279,15 @@ def measure(name, c, steps, warmup, torch, ops, device, world, rank, stream, com
     H, scale = c["H"], c["scale"]
     q, gate, qdyn = x["query"], x["gate"], x["qdyn"]
     kv = bool(c.get("kv"))
+    onorm = int(c.get("out_norm", 0))
+    # count-prior biases log(count_s) of block sources (model.py:1045-1069)
+    bias = (torch.log(torch.arange(1, c["S"] + 1, device=device, dtype=torch.float32))
+            if c.get("bias") else None)
 
     def fwd():
         if kv:
             return ops.lrid_kv_read(x["values"], x["weight"], q, gate, qdyn, None, H, scale, True, 0, True)
-        return ops.lrid_read(x["values"], x["keys"], q, gate, qdyn, None, H, scale, True, 0)
+        return ops.lrid_read(x["values"], x["keys"], q, gate, qdyn, bias, H, scale, True, onorm)
 
     def bwd(*fo):
         if kv:
@@ -286,9 +296,9 @@ def measure(name, c, steps, warmup, torch, ops, device, world, rank, stream, com
                                           x["grad"], out, inv, H, scale, True, 0, True)
             # (dV, dW, dq, dgate, ...): the summed parameter gradients are dW, dq, dgate
             return [r[1], r[2]] + ([r[3]] if qdyn is not None else [])
-        r = ops.lrid_read_backward(x["values"], x["keys"], q, gate, qdyn, None, x["grad"], fo[0], fo[1],
-                                   H, scale, True, 0)
-        return [r[2]] + ([r[3]] if qdyn is not None else [])
+        r = ops.lrid_read_backward(x["values"], x["keys"], q, gate, qdyn, bias, x["grad"], fo[0], fo[1],
+                                   H, scale, True, onorm)
+        return [r[2]] + ([r[3]] if qdyn is not None else []) + ([r[5]] if bias is not None else [])
 
     from attnres_b200.sharding import allreduce_param_grads
 
@@ -431,10 +441,13 @@ def main():
                     ops.lrid_kv_read_backward(x["values"], x["weight"], keys, vinv, alpha, x["query"], None, None,
                                               None, x["grad"], out, inv, H, scale, True, 0, True)
                 else:
-                    out, inv = ops.lrid_read(x["values"], x["keys"], x["query"], x["gate"], x["qdyn"], None, H,
-                                             scale, True, 0)
-                    ops.lrid_read_backward(x["values"], x["keys"], x["query"], x["gate"], x["qdyn"], None,
-                                           x["grad"], out, inv, H, scale, True, 0)
+                    onorm = int(c.get("out_norm", 0))
+                    bias = (torch.log(torch.arange(1, c["S"] + 1, device=device, dtype=torch.float32))
+                            if c.get("bias") else None)
+                    out, inv = ops.lrid_read(x["values"], x["keys"], x["query"], x["gate"], x["qdyn"], bias, H,
+                                             scale, True, onorm)
+                    ops.lrid_read_backward(x["values"], x["keys"], x["query"], x["gate"], x["qdyn"], bias,
+                                           x["grad"], out, inv, H, scale, True, onorm)
         torch.cuda.synchronize()
         if rank == 0:
             print(json.dumps({"profile_run": True, "config": args.config}), flush=True)
@@ -562,56 +575,16 @@ def aux_measurements(c, stream, comm, torch, ops, device, world, rank, hbm, peak
         aux[name] = r
         del x
         torch.cuda.empty_cache()
-    aux["config2_model_read"] = model_read_rate(c, stream, torch, ops, device, rank, hbm)
+    cn = CONFIGS["config2_norm"]
+    x, t = measure("config2_norm", cn, 400, 10, torch, ops, device, world, rank, stream, comm)
+    r = rooflines(cn, t, hbm, world)
+    r["what"] = ("the read model.py issues by default (attnres_fuse_read_norm=True and the count prior, model.py:90, "
+                 ":2238-2244): output RMS norm per head and count-prior logit biases, config-2 shape")
+    aux["config2_model_read"] = r
+    del x
+    torch.cuda.empty_cache()
     aux.update(block_summary_and_phase2(c, stream, torch, device, hbm))
     return aux
-
-
-def model_read_rate(c, stream, torch, ops, device, rank, hbm):
-    """The read that model.py issues by default (attnres_fuse_read_norm=True and
-    the count prior, model.py:90, :2238-2244): output RMS norm per head and
-    per-source logit biases, at the config-2 shape, fwd+bwd."""
-    x = make_inputs(c, device, torch, seed=99 + rank)
-    H, scale = c["H"], c["scale"]
-    bias = torch.log(torch.arange(1, c["S"] + 1, device=device, dtype=torch.float32))
-
-    def fwd():
-        return ops.lrid_read(x["values"], x["keys"], x["query"], None, None, bias, H, scale, True, 1)
-
-    def bwd(fo):
-        return ops.lrid_read_backward(x["values"], x["keys"], x["query"], None, None, bias, x["grad"], fo[0],
-                                      fo[1], H, scale, True, 1)
-
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            bwd(fwd())
-    torch.cuda.synchronize()
-    gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gf, stream=stream):
-        fo = fwd()
-    with torch.cuda.graph(gb, stream=stream):
-        bwd(fo)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    n = 200
-    with torch.cuda.stream(stream):
-        for _ in range(5):
-            gf.replay()
-            gb.replay()
-        ev[0].record(stream)
-        for _ in range(n):
-            gf.replay()
-            gb.replay()
-        ev[1].record(stream)
-    torch.cuda.synchronize()
-    ms = ev[0].elapsed_time(ev[1]) / n
-    tokens = c["B"] * c["T"]
-    fwd_b, bwd_b = algorithmic_bytes(c)
-    # the norm adds the normed output read in the backward and the inverse rms
-    fwd_b, bwd_b = fwd_b + 4, bwd_b + c["D"] * 2 + 4
-    return {"what": "LRID read with output RMS norm (per head) and count-prior logit biases, config-2 shape",
-            "tokens_per_s": tokens / (ms * 1e-3), "ms_per_step": ms,
-            "step_frac": tokens * (fwd_b + bwd_b) / (ms * 1e-3) / 1e9 / hbm,
-            "algorithmic_bytes_per_token": {"fwd": fwd_b, "bwd": bwd_b}}
 
 
 def block_summary_and_phase2(c, stream, torch, device, hbm):
