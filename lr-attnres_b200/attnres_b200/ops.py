@@ -1546,31 +1546,38 @@ def lrid_fused_projection_backward(x: Tensor, weight: Tensor, key: Tensor, key_i
     n = x.numel() // x.size(-1)
     x2 = x.reshape(n, x.size(-1))
     w = weight.to(dt)
-    ncols = output_dim + rank + query_rank
-    # gradient of the projected columns [n, output_dim + rank + query_rank]
-    gp = torch.zeros((n, ncols), device=x.device, dtype=dt)
+    kq_rows = slice(output_dim, output_dim + rank + query_rank)
+    dw = torch.zeros_like(weight)
+    dx = None
+    # the gradient of each column block goes through its own GEMMs, accumulated
+    # in place (no [n, output + rank] gradient buffer)
+    blocks = []
     if grad_output is not None:
-        gp[:, :output_dim] = grad_output.reshape(n, output_dim)
+        blocks.append((slice(0, output_dim), grad_output.to(dt).reshape(n, output_dim)))
     if grad_key is not None:
         gk = grad_key.to(dt).reshape(n, rank).contiguous()
         if key_norm:
-            # the pre-norm key columns, re-projected (an [n, rank] GEMM), so the
-            # norm backward works from them in fp32 as torch's rms_norm does
-            kraw = torch.matmul(x2, w[output_dim:output_dim + rank].t())
-            kview = gp[:, output_dim:output_dim + rank]
+            # the pre-norm key columns, recomputed with the forward's own
+            # [n, rank + query_rank] GEMM (bitwise the values the saved inverse
+            # rms belongs to), so the norm backward works from them in fp32
+            kraw = torch.matmul(x2, w[kq_rows].t())
+            gkn = torch.empty((n, rank), device=x.device, dtype=dt)
             with torch.cuda.device(x.device):
                 rc = N.load().attnres_head_rms_norm_backward(n, rank, num_heads, _dtype_code(dt), _ptr(gk),
-                                                             _ptr(kraw), kraw.stride(0), _ptr(key_inv), _ptr(kview),
-                                                             gp.stride(0), _stream_ptr(x.device))
+                                                             _ptr(kraw), kraw.stride(0), _ptr(key_inv), _ptr(gkn),
+                                                             rank, _stream_ptr(x.device))
             N.check(rc, "attnres_head_rms_norm_backward")
-        else:
-            gp[:, output_dim:output_dim + rank] = gk
+            gk = gkn
+        blocks.append((slice(output_dim, output_dim + rank), gk))
     if grad_query is not None and query_rank:
-        gp[:, output_dim + rank:] = grad_query.reshape(n, query_rank)
-    dx = torch.matmul(gp, w[:ncols]).reshape(x.shape)
-    dw = torch.zeros_like(weight)
-    dw[:ncols] = torch.matmul(gp.t(), x2).to(weight.dtype)
-    return dx, dw
+        blocks.append((slice(output_dim + rank, output_dim + rank + query_rank),
+                       grad_query.to(dt).reshape(n, query_rank)))
+    for rows, g in blocks:
+        dx = torch.matmul(g, w[rows]) if dx is None else torch.addmm(dx, g, w[rows])
+        dw[rows] = torch.matmul(g.t(), x2).to(weight.dtype)
+    if dx is None:
+        dx = torch.zeros_like(x2)
+    return dx.reshape(x.shape), dw
 
 
 @lrid_fused_projection_backward.register_fake
