@@ -6,7 +6,9 @@ its generic block path, model.py:2225-2620) for one family of settings:
 fused output projections (`LRIDFusedProjection`, model.py:316-388, fused-key
 layout), static depth queries, the block-count logit prior (legacy beta),
 count / sqrt block averaging (legacy alpha), per-head key norm, rotary
-embeddings, q/k norm, SwiGLU MLPs and RMS norms before or after each sublayer.
+embeddings, q/k norm, SwiGLU MLPs and RMS norms before or after each sublayer;
+or, with `lrid_key_from_output_tail` (model.py:101, :377-378, :418-419), keys
+that are the last `lrid_rank` columns of each source's value.
 Module and parameter names follow the reference, so a reference state_dict
 loads into it (tests/test_gpt_model.py checks the forward against OBPM).
 
@@ -45,6 +47,8 @@ class GPTConfig:
     attnres_fuse_read_norm: bool = True
     lrid_rank: int = 64
     lrid_num_heads: int = 2
+    lrid_key_from_output_tail: bool = False
+    pad_vocab_to: int = 64
     attn_res_query_init: str = "zero"
     fused: bool = True
 
@@ -85,16 +89,24 @@ class RotaryEmbedding(nn.Module):
 
 class LRIDFusedProjection(nn.Module):
     """Output projection emitting the sublayer output and its LRID key (the
-    reference's fused-key layout: one weight [output + rank, input])."""
+    reference's fused-key layout: one weight [output + rank, input]; with the
+    output-tail key, weight [output, input] and key = output[..., -rank:])."""
 
     def __init__(self, cfg: GPTConfig, input_dim: int, output_dim: int):
         super().__init__()
         self.cfg = cfg
         self.output_dim = output_dim
-        self.proj = nn.Linear(input_dim, output_dim + cfg.lrid_rank, bias=False)
+        extra = 0 if cfg.lrid_key_from_output_tail else cfg.lrid_rank
+        self.proj = nn.Linear(input_dim, output_dim + extra, bias=False)
 
     def forward(self, x: Tensor):
         c = self.cfg
+        if c.lrid_key_from_output_tail:
+            out = self.proj(x)
+            # the fused read takes the key as a strided view of the output rows;
+            # the PyTorch path copies it like the reference (model.py:377-378)
+            key = out[..., -c.lrid_rank:]
+            return out, (key if c.fused else key.contiguous())
         if c.fused:
             from .ops import lrid_fused_projection_forward
 
@@ -109,14 +121,18 @@ class LRIDFusedProjection(nn.Module):
 
 
 class LRIDSourceKeyProjection(nn.Module):
-    """Key of the embedding source (model.py:391-423): proj(x), per-head normed."""
+    """Key of the embedding source (model.py:391-423): proj(x), per-head normed,
+    or the last `lrid_rank` columns of x with the output-tail key."""
 
     def __init__(self, cfg: GPTConfig):
         super().__init__()
         self.cfg = cfg
-        self.proj = nn.Linear(cfg.n_embd, cfg.lrid_rank, bias=False)
+        self.proj = None if cfg.lrid_key_from_output_tail else nn.Linear(cfg.n_embd, cfg.lrid_rank, bias=False)
 
     def forward(self, x: Tensor) -> Tensor:
+        if self.proj is None:
+            key = x[..., -self.cfg.lrid_rank:]
+            return key if self.cfg.fused else key.contiguous()
         key = self.proj(x)
         return norm_heads(key, self.cfg.lrid_num_heads) if self.cfg.attnres_key_norm else key
 
@@ -274,4 +290,17 @@ class GPT(nn.Module):
         x = read(2 * c.n_layer)
         if not fused_read_norm:
             x = norm(x)
-        return x if return_hidden else self.lm_head(x)
+        return x if return_hidden else self.logits(x)
+
+    def logits(self, x: Tensor) -> Tensor:
+        """lm_head(x). With a vocabulary that is not a multiple of
+        `pad_vocab_to` (the reference's 100 277 is odd) the logit rows are not
+        16-byte aligned and the library GEMMs fall back to slow kernels, so
+        the logits are computed against the weight padded with zero rows and
+        returned as the [..., :vocab] view: the same values; the pad's backward
+        drops the padding's gradient. Both read paths do this."""
+        w = self.lm_head.weight
+        pad = -w.size(0) % self.cfg.pad_vocab_to if self.cfg.pad_vocab_to > 1 else 0
+        if pad == 0:
+            return self.lm_head(x)
+        return F.linear(x, F.pad(w, (0, 0, 0, pad)))[..., :w.size(0)]

@@ -23,6 +23,7 @@ SETTINGS = [
     dict(norm_pos="after", lrid_num_heads=2, attnres_num_blocks=2, attnres_block_average_mode="count"),
     dict(norm_pos="before", lrid_num_heads=2, attnres_num_blocks=3, attnres_block_average_mode="sqrt"),
     dict(norm_pos="after", lrid_num_heads=1, attnres_num_blocks=4, attnres_block_count_prior=False),
+    dict(norm_pos="before", lrid_num_heads=2, attnres_num_blocks=2, lrid_key_from_output_tail=True),
 ]
 
 
@@ -47,6 +48,12 @@ def test_gpt_torch_path_matches_reference_model(kw):
     missing, unexpected = gpt.load_state_dict(ref.state_dict(), strict=False)
     assert not missing and not unexpected, (missing, unexpected)
     idx = torch.randint(0, common["vocab_size"], (2, common["block_size"]), generator=torch.Generator().manual_seed(4))
+    if kw.get("lrid_key_from_output_tail"):
+        # tests/test_attnres_ops.py:1306-1327: no key columns, key = value tail
+        assert gpt.transformer.layers[0].attn.c_proj.proj.out_features == common["n_embd"]
+        with torch.no_grad():
+            value, key = gpt.transformer.layers[0].attn.c_proj(torch.randn(2, 8, common["n_embd"]))
+        assert key.is_contiguous() and torch.equal(key, value[..., -common["lrid_rank"]:])
     a, b = ref(idx), gpt(idx)
     torch.testing.assert_close(b, a, rtol=1e-5, atol=1e-6)
     a.float().square().mean().backward()

@@ -14,7 +14,8 @@ from gpu_helpers import assert_close
 pytestmark = pytest.mark.gpu
 
 KW = [dict(norm_pos="after", lrid_num_heads=2, attnres_num_blocks=3),
-      dict(norm_pos="before", lrid_num_heads=1, attnres_num_blocks=4)]
+      dict(norm_pos="before", lrid_num_heads=1, attnres_num_blocks=4),
+      dict(norm_pos="before", lrid_num_heads=2, attnres_num_blocks=2, lrid_key_from_output_tail=True)]
 COMMON = dict(n_layer=4, n_head=4, n_embd=512, vocab_size=301, block_size=64, lrid_rank=64,
               attn_res_query_init="normal")
 
