@@ -739,14 +739,15 @@ def _kv_project(values, weight, value_norm):
 
 
 def _kv_fused_forward(values, weight, query, bias, H, scale, key_norm, value_norm):
-    """The one-kernel key-from-value forward (projection + read, V streamed
-    through shared memory twice per 8-token tile with the second pass served
-    from L2); returns (out, keys [S, *lead, R], value_inv_rms [S, N],
+    """The one-kernel key-from-value forward (projection, softmax and weighted
+    sum with V read from HBM once: clusters of value_dim / 512 CTAs, W held in
+    tensor memory, partial keys reduce-scattered through distributed shared
+    memory); returns (out, keys [S, *lead, R], value_inv_rms [S, N],
     alpha [N, H, S]), or None when it is not selected or the shapes are outside
     the kernel. It is selected with ATTNRES_KV_FWD=one: at config 4 it measures
-    6.9-8.0 ms against 3.4 ms for the projection kernel followed by the read
-    kernel (its consumers are latency-bound), so the two-kernel path is the
-    default."""
+    4.6 ms against 3.4 ms for the projection kernel followed by the read kernel
+    (a ring stage waits ~10 us for its logits to return through the cluster),
+    so the two-kernel path is the default."""
     if os.environ.get("ATTNRES_KV_FWD", "") != "one":
         return None
     S, d, R = len(values), values[0].size(-1), weight.size(0)

@@ -164,33 +164,54 @@ def test_kv_fused_projection_backward_is_deterministic():
 
 
 @pytest.mark.parametrize("S,N,D,H,bias,dtype", [
-    (17, 1000, 2048, 1, False, torch.bfloat16),   # config-4 rows
-    (32, 77, 512, 4, False, torch.bfloat16),      # two full 16-source groups, ragged tile
-    (3, 301, 256, 2, True, torch.float16),        # logit biases, ragged last tile
+    (17, 1000, 2048, 1, False, torch.bfloat16),   # config-4 rows: clusters of 4
+    (32, 77, 1024, 4, False, torch.bfloat16),     # 32 sources, clusters of 2, ragged tile
+    (5, 33, 2048, 2, True, torch.bfloat16),       # logit biases, one partial tile
+    (3, 301, 4096, 2, True, torch.float16),       # clusters of 8, ragged last tile
 ])
 def test_kv_one_kernel_forward_matches_two_pass(kernel_path, monkeypatch, S, N, D, H, bias, dtype):
     """The one-kernel key-from-value forward (projection, softmax and weighted
-    sum in one pass of the tile) against the projection kernel followed by the
-    read kernel: out, the saved keys, value inverse rms and softmax weights."""
+    sum with V read once) against the projection kernel followed by the read
+    kernel: out, the saved keys, value inverse rms and softmax weights. The
+    one-kernel call is made directly, so a shape it refused would fail here
+    instead of silently comparing the two-kernel path with itself."""
     if kernel_path != "auto":
         pytest.skip("one kernel path is enough")
-    ops = torch.ops.attnres
-    import attnres_b200  # noqa: F401
+    from attnres_b200 import _native, ops as O
 
     torch.manual_seed(S + N)
     values = [torch.randn(1, N, D, device="cuda", dtype=dtype) for _ in range(S)]
     w = (torch.randn(64, D, device="cuda") / D ** 0.5).to(dtype)
     q = (torch.randn(H, 64 // H, device="cuda") * 0.5).to(dtype)
     b = torch.randn(S, device="cuda") if bias else None
-    res = {}
-    for mode in ("one", "twopass"):  # ATTNRES_KV_FWD: the one-kernel forward, or the default
-        monkeypatch.setenv("ATTNRES_KV_FWD", mode)
-        out, _, keys, inv, alpha = ops.lrid_kv_read(values, w, q, None, None, b, H, 0.25, True, 0, True)
-        torch.cuda.synchronize()
-        res[mode] = (out, keys, inv, alpha)
-    (o1, k1, i1, a1), (o2, k2, i2, a2) = res["one"], res["twopass"]
+    _native.device_status(reset=True)
+    monkeypatch.setenv("ATTNRES_KV_FWD", "one")
+    fused = O._kv_fused_forward(values, w, q, b, H, 0.25, True, True)
+    assert fused is not None, "the one-kernel forward refused a shape it supports"
+    o1, k1, i1, a1 = fused
+    torch.cuda.synchronize()
+    assert _native.device_status(reset=True) == 0
+    monkeypatch.setenv("ATTNRES_KV_FWD", "twopass")
+    o2, _, k2, i2, a2 = torch.ops.attnres.lrid_kv_read(values, w, q, None, None, b, H, 0.25, True, 0, True)
+    torch.cuda.synchronize()
     assert_close("out", to_np(o1), to_np(o2), dtype)
     assert_close("keys", to_np(k1), to_np(k2), dtype)
     torch.testing.assert_close(i1, i2, rtol=1e-5, atol=0)
-    # a key one bf16 ulp apart (fp32 sums in another order) moves its weights by ~1e-4
-    torch.testing.assert_close(a1, a2, rtol=1e-3, atol=1e-5)
+    # each path's weights are the softmax of its own saved keys (tight) ...
+    for keys, alpha in ((k1, a1), (k2, a2)):
+        torch.testing.assert_close(alpha, _alpha_from_keys(keys, q, b, H, 0.25), rtol=1e-4, atol=1e-6)
+    # ... and the keys of the two paths may differ by one bf16 ulp (fp32 partial
+    # sums added in another order), which moves a weight by up to ~0.5 %
+    torch.testing.assert_close(a1, a2, rtol=1e-2, atol=1e-5)
+
+
+def _alpha_from_keys(keys, q, bias, H, scale):
+    """Softmax over sources of the per-head key-normed logits, in fp32, from
+    saved keys [S, ..., R] -> [N, H, S]."""
+    S, R = keys.size(0), keys.size(-1)
+    k = keys.float().reshape(S, -1, H, R // H)
+    k = k * torch.rsqrt(k.square().mean(-1, keepdim=True) + RMS_EPS)
+    logits = (k * q.float().reshape(1, 1, H, R // H)).sum(-1) * scale
+    if bias is not None:
+        logits = logits + bias.float().reshape(S, 1, 1)
+    return torch.softmax(logits, dim=0).permute(1, 2, 0)
