@@ -59,7 +59,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", choices=sorted(CONFIGS), default="config2")
-    p.add_argument("--e2e-steps", type=int, default=12)
+    p.add_argument("--e2e-steps", type=int, default=40)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-aux", action="store_true", help="skip the config-3/4 and secondary measurements")
     p.add_argument("--profile", action="store_true",
