@@ -1,8 +1,10 @@
 """GPU parity of LRIDFusedProjection.forward (model.py:363-388, fused-key
-layout) against the reference's own composition: one linear projection, the
+layout) against the reference's own composition -- one linear projection, the
 output columns split off, the key columns normalised per head by
-_norm_lrid_key (model.py:33-36), the query columns split off; forward and the
-gradients of x and of the projection weight."""
+_norm_lrid_key (model.py:33-36), the query columns split off -- evaluated in
+float64 from the same (rounded) inputs: forward and the gradients of x and of
+the projection weight. fp32 is held to 1e-5 (the weight gradient, a sum over
+all tokens, to 1e-5 of its scale); 16-bit to the output rounding."""
 import pytest
 import torch
 
@@ -18,7 +20,8 @@ def _ref(x, w, d, R, H, key_norm, Rq):
     key = projected[..., d:d + R]
     if key_norm:
         ks = key.shape
-        key = F.rms_norm(key.reshape(*ks[:-1], H, ks[-1] // H), (ks[-1] // H,)).reshape(ks)
+        # F.rms_norm's default eps for fp32 / 16-bit inputs, which the model uses
+        key = F.rms_norm(key.reshape(*ks[:-1], H, ks[-1] // H), (ks[-1] // H,), eps=RMS_EPS).reshape(ks)
     query = projected[..., d + R:d + R + Rq] if Rq else None
     return out, key, query
 
@@ -33,20 +36,21 @@ def test_fused_projection_matches_reference(dtype, d, R, H, key_norm, Rq):
     x = torch.randn(B, T, din, device="cuda", dtype=dtype, requires_grad=True)
     w = (torch.randn(d + R + Rq, din, device="cuda") / din ** 0.5).to(dtype).requires_grad_(True)
     res = A.lrid_fused_projection_forward(x, w, d, R, H, key_norm, Rq)
-    x2 = x.detach().clone().requires_grad_(True)
-    w2 = w.detach().clone().requires_grad_(True)
-    ref = _ref(x2, w2, d, R, H, key_norm, Rq)
-    tol = dict(rtol=1e-4, atol=1e-4) if dtype == torch.float32 else dict(rtol=2e-2, atol=2e-2)
+    x64 = x.detach().double().requires_grad_(True)
+    w64 = w.detach().double().requires_grad_(True)
+    ref = _ref(x64, w64, d, R, H, key_norm, Rq)
+    if dtype == torch.float32:
+        tol, wtol = dict(rtol=1e-5, atol=1e-5), dict(rtol=1e-5, atol=1e-5 * (B * T) ** 0.5)
+    else:
+        tol, wtol = dict(rtol=2e-2, atol=2e-2), dict(rtol=2e-2, atol=2e-2 * (B * T) ** 0.5)
     for a, b in zip(res, ref):
-        torch.testing.assert_close(a, b, **tol)
-    grads = [torch.randn_like(t) for t in ref if t is not None]
+        torch.testing.assert_close(a.double(), b, **tol)
+    grads = [torch.randn_like(t, dtype=dtype) for t in ref if t is not None]
     torch.autograd.backward([t for t in res], grads)
-    torch.autograd.backward([t for t in ref if t is not None], grads)
-    torch.testing.assert_close(x.grad, x2.grad, **tol)
-    # the weight gradient sums over all B*T tokens: bf16 rounding of the
-    # per-token terms grows like sqrt(B*T)
-    wtol = tol if dtype == torch.float32 else dict(rtol=2e-2, atol=2e-2 * (B * T) ** 0.5)
-    torch.testing.assert_close(w.grad, w2.grad, **wtol)
+    torch.autograd.backward([t for t in ref if t is not None], [g.double() for g in grads])
+    torch.testing.assert_close(x.grad.double(), x64.grad, **tol)
+    # the weight gradient sums over all B*T tokens: its rounding grows like sqrt(B*T)
+    torch.testing.assert_close(w.grad.double(), w64.grad, **wtol)
 
 
 def test_head_rms_norm_reads_a_strided_key_slice():
