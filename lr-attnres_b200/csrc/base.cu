@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "plan.h"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -359,16 +360,13 @@ static cudaError_t base_shape(int dtype, const BasePlan& p, bool bwd, BaseShape*
   bs->smem = base_smem(p, bs->block);
   cudaError_t e;
   if (bs->smem > 48 * 1024) {
-    e = cudaFuncSetAttribute(bs->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(bs->smem));
+    e = ensure_dynamic_smem(reinterpret_cast<const void*>(bs->fn), static_cast<int>(bs->smem));
     if (e != cudaSuccess) return e;
   }
-  int per_sm = 0, dev = 0, nsm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bs->fn, bs->block, bs->smem);
+  int per_sm = 0, nsm = 0;
+  e = cached_occupancy(&per_sm, reinterpret_cast<const void*>(bs->fn), bs->block, bs->smem);
   if (e != cudaSuccess) return e;
-  e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  e = cached_sm_count(&nsm);
   if (e != cudaSuccess) return e;
   if (per_sm <= 0) return cudaErrorInvalidConfiguration;
   const long long cap = static_cast<long long>(nsm) * per_sm;

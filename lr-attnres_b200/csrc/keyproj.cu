@@ -24,6 +24,7 @@
 #include "plan.h"
 #include "tma.cuh"
 #include "umma.cuh"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -342,10 +343,8 @@ cudaError_t keyproj_launch(int S, long long N, int d, int R, int dtype, const vo
   // keys / inv_rms are dense [S][N][R] / [S][N]
   *used_tc = false;
   if (N == 0) return cudaSuccess;
-  int dev = 0, nsm = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  int nsm = 0;
+  cudaError_t e = cached_sm_count(&nsm);
   if (e != cudaSuccess) return e;
   if (allow_tc && tc_eligible(S, N, d, R, dtype, values, vstr, w, w_stride)) {
     KeyProjArgs a{};
@@ -369,10 +368,10 @@ cudaError_t keyproj_launch(int S, long long N, int d, int R, int dtype, const vo
                 (static_cast<uint32_t>(kKpRows >> 4) << 24);
       const size_t smem = 1024 + kKpStages * (kKpRows + R) * kKpK * 2 + 256;
       auto fn = dtype == ATTNRES_DTYPE_BF16 ? keyproj_tc_kernel<__nv_bfloat16> : keyproj_tc_kernel<__half>;
-      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      e = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       int per_sm = 0;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 192, smem);
+      e = cached_occupancy(&per_sm, reinterpret_cast<const void*>(fn), 192, smem);
       if (e != cudaSuccess) return e;
       per_sm = std::max(1, std::min(per_sm, 2));
       const long long grid = std::min<long long>(a.ntiles, static_cast<long long>(nsm) * per_sm);

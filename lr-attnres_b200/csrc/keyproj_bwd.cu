@@ -42,6 +42,7 @@
 #include "plan.h"
 #include "tma.cuh"
 #include "umma.cuh"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -417,9 +418,8 @@ static bool kpb_shape(int S, long long N, int d, int R, int H, int dtype, int* n
   if (dtype == ATTNRES_DTYPE_F32 || R != kKpbR || S < 1 || S > kKpbMaxSources || N < 1) return false;
   if (H < 1 || d % kKpbCols || d % H || (d / H) % kKpbCols || N > 0x7fffffffLL) return false;
   if (encode_fn() == nullptr) return false;
-  int dev = 0, nsm = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
+  int nsm = 0;
+  if (cached_sm_count(&nsm) != cudaSuccess) return false;
   *nch = d / kKpbCols;
   *ntt = static_cast<int>((N + kKpbRows - 1) / kKpbRows);
   *G = std::max(1, std::min(nsm / *nch, *ntt));
@@ -503,7 +503,7 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
   a.idesc_dw = umma_idesc_f16(ab, 1, 1, kKpbCols, kKpbR);
   const size_t smem = kKpbSmem;
   auto fn = bf ? keyproj_bwd_tc_kernel<__nv_bfloat16> : keyproj_bwd_tc_kernel<__half>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   fn<<<nch * G, kKpbThreads, smem, st>>>(a);
   e = cudaGetLastError();

@@ -44,6 +44,7 @@
 #include "plan.h"
 #include "tma.cuh"
 #include "umma.cuh"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -715,10 +716,8 @@ bool kvfused_eligible(int S, long long N, int d, int R, int H, int dtype, const 
   if (!aligned16p(w) || (w_stride * 2) % 16) return *why = "weight rows must be 16-byte aligned", false;
   for (int s = 0; s < S; ++s)
     if (!aligned16p(values[s]) || (vstr[s] * 2) % 16) return *why = "value rows must be 16-byte aligned", false;
-  int dev = 0, cap = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&cap, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-    return *why = "no device", false;
+  int cap = 0;
+  if (cached_smem_optin(&cap) != cudaSuccess) return *why = "no device", false;
   if (static_cast<size_t>(cap) < kvf_fixed_bytes() + 2 * kKvStageBytes) return *why = "not enough shared memory", false;
   return encode_fn() != nullptr || (*why = "no cuTensorMapEncodeTiled", false);
 }
@@ -751,11 +750,10 @@ cudaError_t kvfused_forward_launch(int S, long long N, int d, int H, int dtype, 
   a.key_eps = key_eps;
   a.scale = scale;
   a.idesc = umma_idesc_f16(dtype == ATTNRES_DTYPE_BF16 ? 1u : 0u, 0u, 0u, kKvR, kKvT);
-  int dev = 0, cap = 0, nsm = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  int cap = 0, nsm = 0;
+  cudaError_t e = cached_smem_optin(&cap);
   if (e != cudaSuccess) return e;
-  if ((e = cudaDeviceGetAttribute(&cap, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
-  if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  if ((e = cached_sm_count(&nsm)) != cudaSuccess) return e;
   const size_t fixed = kvf_fixed_bytes();
   a.stages = static_cast<int>(std::min<size_t>(kKvMaxStages, (static_cast<size_t>(cap) - fixed) / kKvStageBytes));
   if (a.stages < 2) return cudaErrorInvalidConfiguration;
@@ -767,7 +765,7 @@ cudaError_t kvfused_forward_launch(int S, long long N, int d, int H, int dtype, 
     case 2: fn = bf ? kvfused_fwd_kernel<__nv_bfloat16, 2> : kvfused_fwd_kernel<__half, 2>; break;
     default: fn = bf ? kvfused_fwd_kernel<__nv_bfloat16, 4> : kvfused_fwd_kernel<__half, 4>; break;
   }
-  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
   cfg.blockDim = dim3(kKvThreads);

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "plan.h"
 #include "lrid_args.cuh"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -520,17 +521,8 @@ struct LaunchShape {
 };
 
 static int device_sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  static std::mutex mu;
-  static std::unordered_map<int, int> cache;
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = cache.find(dev);
-  if (it != cache.end()) return it->second;
   int n = 0;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-  cache[dev] = n;
-  return n;
+  return cached_sm_count(&n) == cudaSuccess ? n : 0;
 }
 
 // Launch geometry for one plan; deterministic for a given device and plan, so
@@ -541,12 +533,11 @@ static cudaError_t lrid_launch_shape(int dtype, const LridPlan& p, bool bwd, Lau
   ls->smem = lrid_smem_bytes(p, ls->block, bwd);
   cudaError_t e = cudaSuccess;
   if (ls->smem > 48 * 1024) {
-    e = cudaFuncSetAttribute(ls->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(ls->smem));
+    e = ensure_dynamic_smem(reinterpret_cast<const void*>(ls->fn), static_cast<int>(ls->smem));
     if (e != cudaSuccess) return e;
   }
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ls->fn, ls->block, ls->smem);
+  e = cached_occupancy(&per_sm, reinterpret_cast<const void*>(ls->fn), ls->block, ls->smem);
   if (e != cudaSuccess) return e;
   const int nsm = device_sm_count();
   if (nsm <= 0 || per_sm <= 0) return cudaErrorInvalidConfiguration;

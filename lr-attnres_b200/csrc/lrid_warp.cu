@@ -7,6 +7,7 @@
 #include <cstring>
 
 #include "lrid_stream.cuh"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -83,9 +84,8 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
   if (base.dk % ke) return false;
   const int kl = base.dk / ke;
   if (!pow2(kl) || kl > 32 || (32 / kl) % base.H) return false;
-  int dev = 0, cap = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  if (cudaDeviceGetAttribute(&cap, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return false;
+  int cap = 0;
+  if (cached_smem_optin(&cap) != cudaSuccess) return false;
   const size_t key_unit = static_cast<size_t>(base.S) * base.R * esz + (has_qd ? base.R * esz : 0);
   const size_t chunk_unit = static_cast<size_t>(base.S) * CW * esz + (bwd ? (has_y ? 2 : 1) * CW * esz : 0);
   const size_t row_unit = (bwd && has_y) ? 2 * static_cast<size_t>(base.d) * esz : 0;
@@ -127,12 +127,10 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
 static cudaError_t stream_shape(int dtype, const LridPlan& p, const TmaLayout& L, bool bwd, int out_norm,
                                 WarpFn* fn, int* grid) {
   *fn = pick_stream(dtype, p, L, bwd, out_norm);
-  cudaError_t e = cudaFuncSetAttribute(*fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_bytes);
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(*fn), L.smem_bytes);
   if (e != cudaSuccess) return e;
-  int dev = 0, nsm = 0;
-  e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  int nsm = 0;
+  e = cached_sm_count(&nsm);
   if (e != cudaSuccess) return e;
   *grid = static_cast<int>(std::max<long long>(1, std::min<long long>(p.N, nsm)));
   return cudaSuccess;

@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "plan.h"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -328,15 +329,13 @@ cudaError_t phase1_launch(int dtype, int logit_dtype, int S, int Q, long long N,
                       sizeof(float) * (A + (bwd ? A * a.wpt : 0) + block / 32 + static_cast<size_t>(a.tpc) * Q);
   cudaError_t e;
   if (smem > 48 * 1024) {
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    e = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  int per_sm = 0, dev = 0, nsm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, block, smem);
+  int per_sm = 0, nsm = 0;
+  e = cached_occupancy(&per_sm, reinterpret_cast<const void*>(fn), block, smem);
   if (e != cudaSuccess) return e;
-  e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  e = cached_sm_count(&nsm);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const long long grid = std::max<long long>(1, std::min<long long>(a.ntiles, static_cast<long long>(nsm) * per_sm));

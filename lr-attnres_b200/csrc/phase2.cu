@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "plan.h"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -283,8 +284,8 @@ static bool phase2_vec(const Phase2Args& a, int esz, bool bwd) {
 
 // dq blocks: token ranges over about 4 CTAs per SM
 static int phase2_wsum_blocks(long long N) {
-  int dev = 0, nsm = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  int nsm = 148;
+  if (cached_sm_count(&nsm) != cudaSuccess) nsm = 148;
   return static_cast<int>(std::max<long long>(1, std::min<long long>(N, 4LL * nsm)));
 }
 

@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "plan.h"
+#include "launch_cache.h"
 
 namespace attnres {
 
@@ -291,8 +292,8 @@ cudaError_t summary_norm_launch(bool bwd, long long rows, int d, int dtype, cons
 }
 
 static int summary_grid(long long n, int vec) {
-  int dev = 0, nsm = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  int nsm = 148;
+  if (cached_sm_count(&nsm) != cudaSuccess) nsm = 148;
   const long long need = (n / vec + 256 * kSummaryUnroll - 1) / (256 * kSummaryUnroll) + 1;
   return static_cast<int>(std::max<long long>(1, std::min<long long>(need, static_cast<long long>(kSummaryCtasPerSm) * nsm)));
 }
