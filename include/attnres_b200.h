@@ -266,6 +266,41 @@ int attnres_lrid_key_projection_backward_tc(int num_sources, int64_t num_tokens,
                                             void* stream);
 
 /*
+ * Key-from-value LRID read backward in one pass over the values (static query,
+ * no output norm): the read backward, the key RMS-norm backward and the key
+ * projection backward fused, so each value row is read once and each value
+ * gradient row written once. keys dtype [S][N][R] and alpha float [N][H][S]
+ * as saved by the forward (attnres_lrid_key_projection + attnres_lrid_forward,
+ * or attnres_lrid_key_from_value_forward); output dtype [N][value_dim] is the
+ * forward's output; query dtype [num_heads * key_dim / num_heads].
+ *   grad_values[s][n]     = alpha g + dKs_s @ W - V_s coef  (dtype, written)
+ *   grad_weight [R][d]    = sum_s dKs_s^T @ V_s            (float, overwritten)
+ *   grad_query [R]        = summed query gradient           (float, overwritten)
+ *   grad_logit_bias [S]   = summed bias gradient, or NULL   (float, overwritten)
+ * The softmax backward uses sum_j alpha_j <g, V_j> = <g, output>, so the
+ * 16-bit output's rounding enters the logit gradient (well inside the 16-bit
+ * tolerance). f16/bf16, key_dim 64, 2..24 sources, num_heads 1/2/4/8,
+ * value_dim / num_heads a multiple of 256, value_dim <= 4096; the workspace
+ * query returns 0 otherwise (use the read backward followed by
+ * attnres_lrid_key_projection_backward_tc). Deterministic. Needs every SM it
+ * launches on at once (one CTA per SM, partners exchange partial dots); a wait
+ * that runs out (~2 s) sets a bit in attnres_device_status(). Replaces the
+ * autograd backward of the read (attnres_ops.py:4725, lrid_read_list_backward)
+ * together with that of model.py:344-356 (rms_norm + value_key_proj).
+ */
+size_t attnres_lrid_key_from_value_backward_workspace_bytes(int num_sources, int64_t num_tokens, int value_dim,
+                                                             int key_dim, int num_heads, int dtype);
+int attnres_lrid_key_from_value_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                         int num_heads, int dtype, const void* const* values,
+                                         const int64_t* value_row_strides, const void* weight,
+                                         int64_t weight_row_stride, const void* keys, int value_norm,
+                                         const float* value_inv_rms, const float* alpha, const void* query,
+                                         float logit_scale, int key_norm, float key_eps, const void* grad_output,
+                                         const void* output, void* const* grad_values, float* grad_weight,
+                                         float* grad_query, float* grad_logit_bias, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+
+/*
  * Block summary of block Attention Residuals, one pass over the rows:
  *   sum = partial + x (partial may be NULL),  source = sum * c
  * with c = *scale_device when scale_device is not NULL (a learned scale,

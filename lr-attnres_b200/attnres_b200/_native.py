@@ -38,6 +38,8 @@ EXPORTED_SYMBOLS = (
     "attnres_lrid_key_from_value_forward",
     "attnres_lrid_key_projection_backward_tc_workspace_bytes",
     "attnres_lrid_key_projection_backward_tc",
+    "attnres_lrid_key_from_value_backward_workspace_bytes",
+    "attnres_lrid_key_from_value_backward",
     "attnres_block_summary_forward",
     "attnres_block_summary_backward_workspace_bytes",
     "attnres_block_summary_backward",
@@ -130,6 +132,17 @@ def load(path=None):
         PP, P, P, P, P, I,           # grad_keys, keys, inv_rms, grad_output, alpha, value_norm
         PP, P, P, SZ,                # grad_values, grad_weight, workspace, workspace bytes
         P,                           # stream
+    ]
+    L.attnres_lrid_key_from_value_backward_workspace_bytes.restype = SZ
+    L.attnres_lrid_key_from_value_backward_workspace_bytes.argtypes = [I, I64, I, I, I, I]
+    L.attnres_lrid_key_from_value_backward.restype = I
+    L.attnres_lrid_key_from_value_backward.argtypes = [
+        I, I64, I, I, I, I,          # S, N, d, R, H, dtype
+        PP, PI64, P, I64,            # values, strides, weight, weight row stride
+        P, I, P, P, P,               # keys, value_norm, value_inv_rms, alpha, query
+        F, I, F, P, P,               # scale, key_norm, key_eps, grad_output, output
+        PP, P, P, P,                 # grad_values, grad_weight, grad_query, grad_logit_bias
+        P, SZ, P,                    # workspace, workspace bytes, stream
     ]
     L.attnres_block_summary_forward.restype = I
     L.attnres_block_summary_forward.argtypes = [I64, I, P, P, P, F, P, P, P]

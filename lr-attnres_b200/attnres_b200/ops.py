@@ -822,6 +822,51 @@ def _(values, key_weight, query, query_gate, query_dynamic, logit_bias, num_head
             v0.new_empty(aux, dtype=torch.float32))
 
 
+def _kv_backward_one_pass(values, key_weight, keys, value_inv_rms, alpha, query, logit_bias, grad_output, output,
+                          H, scale, key_norm, value_norm):
+    """Key-from-value read backward with a static query in one kernel that
+    reads each value row once (the read backward, the key-norm backward and
+    the key-projection backward fused; partial dots exchanged between the
+    column slices of a token tile through cluster shared memory). Selected
+    with ATTNRES_KV_BWD=one: at config 4 it measures 12-16 ms against 5.4 ms
+    for the read backward followed by the tensor-core projection backward (a
+    ring stage stays resident through the exchange round trip), so the
+    two-kernel path is the default. Returns the lrid_kv_read_backward tuple,
+    or None when the shapes are outside the kernel."""
+    S, d, R = len(values), values[0].size(-1), key_weight.size(0)
+    dtype = values[0].dtype
+    n = _ntok(values[0])
+    device = values[0].device
+    with torch.cuda.device(device):
+        L = N.load()
+        ws_bytes = L.attnres_lrid_key_from_value_backward_workspace_bytes(S, n, d, R, int(H), _dtype_code(dtype))
+        if ws_bytes == 0:
+            return None
+        rows, strides = _sources(values, d, dtype)
+        w = key_weight.to(dtype)
+        if w.stride(-1) != 1:
+            w = w.contiguous()
+        q = query.to(dtype).reshape(-1).contiguous()
+        g = grad_output.to(dtype).reshape(n, d).contiguous()
+        out = output.to(dtype).reshape(n, d).contiguous()
+        gv = [torch.empty(v.shape, device=device, dtype=dtype) for v in values]
+        dw = torch.empty((R, d), device=device, dtype=torch.float32)
+        dq = torch.empty((int(H), R // int(H)), device=device, dtype=torch.float32)
+        e = values[0].new_empty((0,), dtype=torch.float32)
+        dbias = torch.empty((S,), device=device, dtype=torch.float32) if logit_bias is not None else None
+        ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8)
+        kd = keys.reshape(S, n, R).contiguous()
+        vinv = value_inv_rms.contiguous()
+        al = alpha.contiguous()
+        rc = L.attnres_lrid_key_from_value_backward(
+            S, n, d, R, int(H), _dtype_code(dtype), N.ptr_array([t.data_ptr() for t in rows]), N.i64_array(strides),
+            _ptr(w), int(w.stride(0)), _ptr(kd), int(bool(value_norm)), _ptr(vinv), _ptr(al), _ptr(q), float(scale), int(bool(key_norm)),
+            F32_EPS, _ptr(g), _ptr(out), N.ptr_array([t.data_ptr() for t in gv]), _ptr(dw), _ptr(dq),
+            _ptr(dbias), _ptr(ws), ws_bytes, _stream_ptr(device))
+    N.check(rc, "attnres_lrid_key_from_value_backward")
+    return gv, dw, dq, e, e.clone(), dbias if dbias is not None else e.clone()
+
+
 @torch.library.custom_op("attnres::lrid_kv_read_backward", mutates_args=())
 def lrid_kv_read_backward(
     values: List[Tensor],
@@ -848,6 +893,12 @@ def lrid_kv_read_backward(
     R = key_weight.size(0)
     dtype = values[0].dtype
     one_pass = int(output_norm) == N.NORM_NONE and alpha.numel() > 1
+    if (one_pass and query is not None and query_gate is None and query_dynamic is None
+            and os.environ.get("ATTNRES_KV_BWD", "tc") == "one"):
+        fused = _kv_backward_one_pass(values, key_weight, keys, value_inv_rms, alpha, query, logit_bias, grad_output,
+                                      normed_output, int(num_heads), logit_scale, key_norm, value_norm)
+        if fused is not None:
+            return fused
     gv, gk, dq, dgate, dqd, dbias = _lrid_backward_impl(
         values, list(keys.unbind(0)), query, query_gate, query_dynamic, logit_bias, grad_output, normed_output,
         output_inv_rms, num_heads, logit_scale, key_norm, int(output_norm), write_dv=not one_pass)

@@ -15,7 +15,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 OUT = os.path.join(HERE, "attnres_b200", "libattnres_b200.so")
 SOURCES = ["abi.cu", "lrid.cu", "lrid_warp.cu", "lrid_stream_fwd.cu", "lrid_stream_bwd_f32.cu",
-           "lrid_stream_bwd_f16.cu", "lrid_stream_bwd_bf16.cu", "base.cu", "keyproj.cu", "kvfused.cu", "keyproj_bwd.cu", "phase1.cu", "phase2.cu", "headnorm.cu", "summary.cu", "noalloc.cu", "launch_cache.cu"]
+           "lrid_stream_bwd_f16.cu", "lrid_stream_bwd_bf16.cu", "base.cu", "keyproj.cu", "kvfused.cu", "keyproj_bwd.cu", "kvbwd.cu", "phase1.cu", "phase2.cu", "headnorm.cu", "summary.cu", "noalloc.cu", "launch_cache.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr"]
 

@@ -147,6 +147,8 @@ int attnres_device_status(unsigned* status, int reset) {
   s3 |= s4;
   if (e == cudaSuccess) e = attnres::read_kvfused_status(&s4, reset != 0);
   s3 |= s4;
+  if (e == cudaSuccess) e = attnres::read_kvbwd_status(&s4, reset != 0);
+  s3 |= s4;
   if (e != cudaSuccess) return cuda_fail(e, "attnres_device_status");
   *status = s1 | s2 | s3;
   return ATTNRES_OK;
@@ -521,6 +523,54 @@ int attnres_lrid_key_projection_backward_tc(int num_sources, int64_t num_tokens,
       weight_row_stride, grad_keys, keys, inv_rms, grad_output, alpha, value_norm, grad_values, grad_weight,
       workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_projection_backward_tc launch");
+  return ATTNRES_OK;
+}
+
+size_t attnres_lrid_key_from_value_backward_workspace_bytes(int num_sources, int64_t num_tokens, int value_dim,
+                                                             int key_dim, int num_heads, int dtype) {
+  return attnres::kvbwd_fused_workspace(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype);
+}
+
+int attnres_lrid_key_from_value_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
+                                         int num_heads, int dtype, const void* const* values,
+                                         const int64_t* value_row_strides, const void* weight,
+                                         int64_t weight_row_stride, const void* keys, int value_norm,
+                                         const float* value_inv_rms, const float* alpha, const void* query,
+                                         float logit_scale, int key_norm, float key_eps, const void* grad_output,
+                                         const void* output, void* const* grad_values, float* grad_weight,
+                                         float* grad_query, float* grad_logit_bias, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  int rc = check_sources(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values,
+                         value_row_strides, nullptr, nullptr, false);
+  if (rc) return rc;
+  if (num_tokens == 0) return ATTNRES_OK;
+  const size_t need = attnres::kvbwd_fused_workspace(num_sources, num_tokens, value_dim, key_dim, num_heads, dtype);
+  if (need == 0)
+    return fail(ATTNRES_ERR_UNSUPPORTED,
+                "one-pass key-from-value backward needs f16/bf16, key_dim 64, 2..24 sources, num_heads 1/2/4/8, "
+                "value_dim/num_heads a multiple of 256, value_dim <= 4096");
+  if (!weight || !keys || !alpha || !query || !grad_output || !output || !grad_values || !grad_weight ||
+      !grad_query || !workspace || (value_norm && !value_inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "one-pass key-from-value backward: NULL buffer");
+  if (workspace_bytes < need)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  if (weight_row_stride < value_dim) return fail(ATTNRES_ERR_INVALID_ARGUMENT, "weight_row_stride < value_dim");
+  if (!aligned16(grad_output) || !aligned16(output) || !aligned16(keys) || !aligned16(workspace) ||
+      !aligned16(weight) || (weight_row_stride * 2) % 16)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT,
+                "grad_output, output, keys, weight rows and workspace must be 16-byte aligned");
+  for (int s = 0; s < num_sources; ++s) {
+    if (!grad_values[s] || !aligned16(grad_values[s]))
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "grad_values[%d] NULL or not 16-byte aligned", s);
+    if (!aligned16(values[s]) || (value_row_strides[s] * 2) % 16)
+      return fail(ATTNRES_ERR_INVALID_ARGUMENT, "values[%d] must be 16-byte aligned with 16-byte row strides", s);
+  }
+  cudaError_t e = attnres::kvbwd_fused_launch(
+      num_sources, num_tokens, value_dim, key_dim, num_heads, dtype, values, value_row_strides, weight,
+      weight_row_stride, keys, value_norm ? value_inv_rms : nullptr, alpha, query, logit_scale, key_norm, key_eps,
+      grad_output, output, grad_values, grad_weight, grad_query, grad_logit_bias, workspace, workspace_bytes,
+      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_key_from_value_backward launch");
   return ATTNRES_OK;
 }
 

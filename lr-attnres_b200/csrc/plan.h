@@ -159,6 +159,18 @@ cudaError_t keyproj_bwd_tc_launch(int S, long long N, int d, int R, int H, int d
                                   float* grad_weight, void* workspace, size_t workspace_bytes, cudaStream_t st);
 cudaError_t read_keyproj_bwd_status(unsigned* status, bool reset);
 
+// Key-from-value read backward in one pass over the values (kvbwd.cu): read
+// backward, key-norm backward and key-projection backward fused, static query.
+// Workspace 0 means the shapes do not fit the kernel.
+size_t kvbwd_fused_workspace(int S, long long N, int d, int R, int H, int dtype);
+cudaError_t kvbwd_fused_launch(int S, long long N, int d, int R, int H, int dtype, const void* const* values,
+                               const int64_t* vstr, const void* w, long long w_stride, const void* keys,
+                               const float* inv_rms, const float* alpha, const void* query, float scale,
+                               int key_norm, float key_eps, const void* g, const void* out,
+                               void* const* grad_values, float* grad_weight, float* grad_query,
+                               float* grad_bias, void* workspace, size_t workspace_bytes, cudaStream_t st);
+cudaError_t read_kvbwd_status(unsigned* status, bool reset);
+
 // Key-from-value read forward in one kernel (kvfused.cu): projection, key
 // norm, softmax and weighted sum; saves keys [S][N][64], value inverse rms
 // [S][N] and alpha [N][H][S] for the backward.

@@ -215,3 +215,54 @@ def _alpha_from_keys(keys, q, bias, H, scale):
     if bias is not None:
         logits = logits + bias.float().reshape(S, 1, 1)
     return torch.softmax(logits, dim=0).permute(1, 2, 0)
+
+
+@pytest.mark.parametrize("S,N,D,H,dtype,value_norm,bias", [
+    (17, 300, 2048, 1, torch.bfloat16, True, False),   # config-4 row shape, ragged last token tile
+    (6, 2500, 1024, 2, torch.float16, True, True),     # two heads, several tiles per slice group, biases
+    (3, 513, 512, 1, torch.bfloat16, False, False),    # no value norm (coef = 0), two column slices
+    (5, 700, 1024, 4, torch.bfloat16, True, True),     # four heads of 256 columns
+    (4, 257, 2048, 8, torch.float16, True, False),     # eight heads
+])
+def test_kv_one_pass_backward_matches_oracle(kernel_path, monkeypatch, S, N, D, H, dtype, value_norm, bias):
+    """The one-pass key-from-value backward (partial dots exchanged between the
+    column slices of a token tile, dKs formed in-kernel, dV/dW on tcgen05)
+    against the oracle, and against the read backward + projection backward it
+    replaces (same saved forward tensors)."""
+    if kernel_path != "auto":
+        pytest.skip("one kernel path is enough for the one-pass backward")
+    import attnres_b200  # noqa: F401
+
+    ops = torch.ops.attnres
+    R = 64
+    inp = make(S, N, D, R, H, seed=S * N + D + H)
+    scale = 1.0 / np.sqrt(R // H)
+    vals = [dev_rows(v, 1, N, dtype, requires_grad=False) for v in inp["values"]]
+    w = torch.tensor(inp["key_weight"], device="cuda").to(dtype)
+    q = torch.tensor(inp["query"], device="cuda").to(dtype)
+    g = dev_rows(inp["grad_output"], 1, N, dtype, requires_grad=False)
+    b = torch.log(torch.arange(1, S + 1, device="cuda", dtype=torch.float32)) * 0.7 if bias else None
+    out, oinv, keys, vinv, alpha = ops.lrid_kv_read(vals, w, q, None, None, b, H, scale, True, 0, value_norm)
+
+    def bwd(path):
+        monkeypatch.setenv("ATTNRES_KV_BWD", path)
+        r = ops.lrid_kv_read_backward(vals, w, keys, vinv, alpha, q, None, None, b, g, out, oinv, H, scale, True,
+                                      0, value_norm)
+        torch.cuda.synchronize()
+        return {"dV": np.stack([to_np(x).reshape(N, D) for x in r[0]]), "dW": to_np(r[1]),
+                "dq": to_np(r[2]).reshape(-1), "dbias": to_np(r[5]) if bias else None}
+
+    one, two = bwd("one"), bwd("tc")
+    kw = {"logit_bias": to_np(b)} if bias else {}
+    v, wr = rounded(inp["values"], dtype), rounded(inp["key_weight"], dtype)
+    ref = oracle.lrid_kv_backward(v, wr, H, scale, True, rounded(inp["grad_output"], dtype), value_norm=value_norm,
+                                  value_eps=RMS_EPS, query=rounded(inp["query"], dtype), **kw)
+    assert_close("dV", one["dV"], ref["dV"], dtype)
+    assert_close("dW", one["dW"], ref["dW"], dtype, sum_terms=N)
+    assert_close("dq", one["dq"], ref["dq"], dtype, sum_terms=N)
+    assert_close("dV (one pass vs two kernels)", one["dV"], two["dV"], dtype)
+    assert_close("dW (one pass vs two kernels)", one["dW"], two["dW"], dtype, sum_terms=N)
+    assert_close("dq (one pass vs two kernels)", one["dq"], two["dq"], dtype, sum_terms=N)
+    if bias:
+        assert_close("dbias", one["dbias"], ref["dbias"], dtype, sum_terms=N)
+        assert_close("dbias (one pass vs two kernels)", one["dbias"], two["dbias"], dtype, sum_terms=N)
