@@ -282,11 +282,15 @@ int attnres_lrid_key_projection_backward_tc(int num_sources, int64_t num_tokens,
  * tolerance). f16/bf16, key_dim 64, 2..24 sources, num_heads 1/2/4/8,
  * value_dim / num_heads a multiple of 256, value_dim <= 4096; the workspace
  * query returns 0 otherwise (use the read backward followed by
- * attnres_lrid_key_projection_backward_tc). Deterministic. Needs every SM it
- * launches on at once (one CTA per SM, partners exchange partial dots); a wait
- * that runs out (~2 s) sets a bit in attnres_device_status(). Replaces the
- * autograd backward of the read (attnres_ops.py:4725, lrid_read_list_backward)
- * together with that of model.py:344-356 (rms_norm + value_key_proj).
+ * attnres_lrid_key_projection_backward_tc). Deterministic. Launched as
+ * thread-block clusters of value_dim / 128 CTAs (16, a non-portable cluster
+ * size, for value_dim 2048) that exchange partial dots through distributed
+ * shared memory; a wait that runs out (~2 s) sets a bit in
+ * attnres_device_status(). Measured slower than the two-kernel path at config
+ * 4 (12-16 ms against 5.4 ms): the exchange round trip keeps each ring stage
+ * resident too long. Replaces the autograd backward of the read
+ * (attnres_ops.py:4725, lrid_read_list_backward) together with that of
+ * model.py:344-356 (rms_norm + value_key_proj).
  */
 size_t attnres_lrid_key_from_value_backward_workspace_bytes(int num_sources, int64_t num_tokens, int value_dim,
                                                              int key_dim, int num_heads, int dtype);
