@@ -14,7 +14,9 @@ are 320 MB per rank, larger than the 126 MB L2, so no flush is needed); `e2e`
 repeats the step through the public Python API with pinned host buffers and
 host<->device copies inside the timed region. `--impl reference` times the CPU
 oracle (a double-precision C restatement of the reference's PyTorch path) on
-the host cores instead.
+the host cores instead; when the reference module sits in baseline/_ref and a
+GPU is visible, its line also carries `reference_gpu`: the reference's own
+GPU path (Triton where it has a kernel) timed on the same workload.
 """
 import argparse
 import json
@@ -176,6 +178,83 @@ def _oracle_inputs(c, n, seed=0):
     return v, k, g, kw
 
 
+REF_MODULE = os.path.join(ROOT, "baseline", "_ref", "attnres_ops.py")
+
+
+def reference_gpu_rate(c, steps=20, warmup=5):
+    """The reference's own GPU path for the workload: its public
+    lrid_attention_residual_read (attnres_ops.py:4852) with its own dispatch
+    (the Triton library op `attnres::lrid_read_list` + backward for a static
+    query, its PyTorch list path for the gated query, attnres_ops.py:4886-4925),
+    forward + backward through autograd on cuda:0, as model.py calls it
+    (model.py:2117-2128; keys from values as model.py:348-356 projects them).
+    Loaded from baseline/_ref, the unmodified module, under its own name; this
+    repository's package is not imported in the reference arm. Returns a dict,
+    or {"unavailable": why}."""
+    if not os.path.exists(REF_MODULE):
+        return {"unavailable": "baseline/_ref/attnres_ops.py absent (the checkout has no setup.py or "
+                               "pyproject.toml, so pip cannot install it; copy the module there)"}
+    import importlib.util
+
+    import torch
+    import torch.nn.functional as F
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    spec = importlib.util.spec_from_file_location("reference_attnres_ops", REF_MODULE)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    S, B, T, D, R, H = c["S"], c["B"], c["T"], c["D"], c["R"], c["H"]
+    bf = torch.bfloat16
+    vals = [torch.randn(B, T, D, device=dev, dtype=bf, generator=gen).requires_grad_() for _ in range(S)]
+    q = (torch.randn(H, R // H, device=dev, generator=gen) * 0.02).requires_grad_()
+    grad = torch.randn(B, T, D, device=dev, dtype=bf, generator=gen)
+    kv = bool(c.get("kv"))
+    if kv:
+        w = (torch.randn(R, D, device=dev, generator=gen) / D ** 0.5).to(bf).requires_grad_()
+        keys = None
+    else:
+        keys = [torch.randn(B, T, R, device=dev, dtype=bf, generator=gen).requires_grad_() for _ in range(S)]
+    gate = qdyn = None
+    if c["query"] == "gated":
+        gate = torch.full((H,), 0.1, device=dev).requires_grad_()
+        qdyn = torch.randn(B, T, H, R // H, device=dev, dtype=bf, generator=gen).requires_grad_()
+
+    def step():
+        ks = [F.linear(F.rms_norm(v, (D,)), w) for v in vals] if kv else keys
+        query = q if gate is None else q.unsqueeze(0).unsqueeze(0) + gate.view(1, 1, H, 1) * qdyn
+        out = ref.lrid_attention_residual_read(vals, ks, query, H, c["scale"], True,
+                                               normalize_output=bool(c.get("out_norm")),
+                                               source_counts=list(range(1, S + 1)) if c.get("bias") else None)
+        out.backward(grad)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if c.get("bias"):
+        route = "count-prior route: PyTorch logits, Triton phase-1 read from logits"
+    elif gate is None and S <= 16 and not kv:
+        route = "Triton library op attnres::lrid_read_list + backward"
+    else:
+        route = "reference PyTorch list path on the GPU"
+    if kv:
+        route += " (keys: F.linear(F.rms_norm(V_s), W_k) per source)"
+    return {"value": B * T / ms * 1e3, "unit": UNIT, "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "device": torch.cuda.get_device_name(dev), "route": route, "dtype": "bf16",
+            "timing": "CUDA events around eager fwd+bwd steps (autograd, as model.py trains)"}
+
+
 def run_reference(args, c):
     """Reference arm: the CPU oracle (fp64 C restatement of the reference's
     PyTorch path, all host threads) over a token sample of the workload per
@@ -215,6 +294,11 @@ def run_reference(args, c):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_aux:
+        try:
+            line["reference_gpu"] = reference_gpu_rate(c)
+        except Exception as e:  # the CPU line stands; say why the GPU leg did not run
+            line["reference_gpu"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     print(json.dumps(line), flush=True)
 
 
