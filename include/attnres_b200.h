@@ -351,6 +351,27 @@ int attnres_block_summary_norm_backward(int64_t num_rows, int row_width, int dty
                                         void* grad_total, void* stream);
 
 /*
+ * Key/query columns of the fused output projection with the key norm in the
+ * GEMM's epilogue: key_query[n, :] = round(x[n, :] @ weight^T) for the
+ * rank + query_rank rows of weight (the projection weight's rows after the
+ * output columns); with key_norm, key[n, h*dk + j] = round(kq[n, h*dk + j] *
+ * inv[n, h]), inv = rsqrt(mean_j kq[n, h*dk + j]^2 + eps) over the rounded
+ * values, dk = rank / num_heads, and key_inv_rms float [N, num_heads].
+ * key_query dtype [N, rank + query_rank] dense, key dtype [N, rank] dense.
+ * Replaces, for the key and query columns, the F.linear of
+ * LRIDFusedProjection.forward (model.py:363-374) and _norm_lrid_key
+ * (model.py:33-36) as applied at model.py:375-379; the output columns stay a
+ * plain GEMM. tcgen05 tensor cores (TMA-fed, accumulators in TMEM, the norm
+ * from TMEM in the epilogue); returns ATTNRES_ERR_UNSUPPORTED, launching
+ * nothing, unless: bf16/fp16, in_dim % 64 == 0, rank + query_rank a multiple
+ * of 16 in [16, 256], dk % 16 == 0 with key_norm, 16-byte aligned rows.
+ */
+int attnres_lrid_fused_key_projection(int64_t num_tokens, int in_dim, int rank, int query_rank, int num_heads,
+                                      int dtype, const void* x, int64_t x_row_stride, const void* weight,
+                                      int64_t weight_row_stride, int key_norm, float eps, void* key_query,
+                                      void* key, float* key_inv_rms, void* stream);
+
+/*
  * Per-head RMS norm of key rows: y[r, h*dk + j] = x[r, h*dk + j] * inv_rms[r, h],
  * inv_rms = rsqrt(mean_j x^2 + eps), dk = width / num_heads, fp32 math, y and
  * grad dense [rows, width]; x may be a strided slice (x_row_stride elements),

@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "attnres_block_summary_norm_backward",
     "attnres_head_rms_norm_forward",
     "attnres_head_rms_norm_backward",
+    "attnres_lrid_fused_key_projection",
     "attnres_phase2_forward",
     "attnres_phase2_backward_workspace_bytes",
     "attnres_phase2_backward",
@@ -156,6 +157,8 @@ def load(path=None):
     L.attnres_block_summary_norm_backward.argtypes = [I64, I, I, P, P, P, P, P, P]
     L.attnres_head_rms_norm_forward.restype = I
     L.attnres_head_rms_norm_forward.argtypes = [I64, I, I, I, P, I64, F, P, P, P]
+    L.attnres_lrid_fused_key_projection.restype = I
+    L.attnres_lrid_fused_key_projection.argtypes = [I64, I, I, I, I, I, P, I64, P, I64, I, F, P, P, P, P]
     L.attnres_head_rms_norm_backward.restype = I
     L.attnres_head_rms_norm_backward.argtypes = [I64, I, I, I, P, P, I64, P, P, I64, P]
     L.attnres_phase2_forward.restype = I

@@ -1550,10 +1550,13 @@ def lrid_fused_projection(x: Tensor, weight: Tensor, output_dim: int, rank: int,
     """The projection x @ weight^T with weight [output_dim + rank + query_rank, in],
     returned as (output [*, output_dim] contiguous, key [*, rank] (per-head rms
     normalised when key_norm), query [*, query_rank] or empty, key inverse rms
-    [N, num_heads] fp32 or empty). The output and the key/query columns come
-    from two library GEMMs straight into their own buffers (the reference's
-    single GEMM is followed by a .contiguous() copy of the output columns); the
-    key norm reads the key columns in place."""
+    [N, num_heads] fp32 or empty). The output columns are a plain library GEMM
+    straight into their own buffer (the reference's single GEMM is followed by a
+    .contiguous() copy of them). The key/query columns, for 16-bit data, come
+    from the tcgen05 projection kernel with the per-head key norm in its
+    epilogue (attnres_lrid_fused_key_projection); for fp32 (no tensor-core
+    path at fp32 accuracy) or shapes outside that kernel, from a second library
+    GEMM and the per-head norm kernel reading the key columns in place."""
     _require_cuda([x, weight], "fused projection inputs")
     dt = x.dtype
     n = x.numel() // x.size(-1)
@@ -1561,8 +1564,16 @@ def lrid_fused_projection(x: Tensor, weight: Tensor, output_dim: int, rank: int,
     w = weight.to(dt)
     lead = x.shape[:-1]
     out = torch.matmul(x2, w[:output_dim].t())
-    kq = torch.matmul(x2, w[output_dim:output_dim + rank + query_rank].t())  # [n, rank + query_rank]
     e = lambda: x.new_empty((0,), dtype=torch.float32)  # noqa: E731
+    tc = _fused_key_projection_tc(x2, w, output_dim, rank, num_heads, key_norm, query_rank)
+    if tc is not None:
+        kq, key, inv = tc
+        query = kq[:, rank:].contiguous() if query_rank else x.new_empty((0,))
+        if not key_norm:
+            key, inv = kq[:, :rank].contiguous(), e()
+        return (out.reshape(*lead, output_dim), key.reshape(*lead, rank),
+                query.reshape(*lead, query_rank) if query_rank else query, inv)
+    kq = torch.matmul(x2, w[output_dim:output_dim + rank + query_rank].t())  # [n, rank + query_rank]
     if key_norm:
         key = torch.empty((n, rank), device=x.device, dtype=dt)
         inv = torch.empty((n, num_heads), device=x.device, dtype=torch.float32)
@@ -1577,6 +1588,30 @@ def lrid_fused_projection(x: Tensor, weight: Tensor, output_dim: int, rank: int,
     query = kq[:, rank:].contiguous() if query_rank else x.new_empty((0,))
     return (out.reshape(*lead, output_dim), key.reshape(*lead, rank),
             query.reshape(*lead, query_rank) if query_rank else query, inv)
+
+
+def _fused_key_projection_tc(x2, w, output_dim, rank, num_heads, key_norm, query_rank, normed=True):
+    """(kq [n, rank + query_rank] pre-norm, key [n, rank] normed or None, inv
+    [n, H] or None) from the tcgen05 projection kernel, or None for fp32 and
+    for shapes outside it (ATTNRES_ERR_UNSUPPORTED, nothing launched)."""
+    if x2.dtype not in (torch.float16, torch.bfloat16) or x2.stride(-1) != 1:
+        return None
+    n = x2.size(0)
+    wk = w[output_dim:output_dim + rank + query_rank]
+    if wk.stride(-1) != 1:
+        return None
+    norm = bool(key_norm) and normed
+    kq = torch.empty((n, rank + query_rank), device=x2.device, dtype=x2.dtype)
+    key = torch.empty((n, rank), device=x2.device, dtype=x2.dtype) if norm else None
+    inv = torch.empty((n, num_heads), device=x2.device, dtype=torch.float32) if norm else None
+    with torch.cuda.device(x2.device):
+        rc = N.load().attnres_lrid_fused_key_projection(
+            n, x2.size(1), rank, query_rank, num_heads, _dtype_code(x2.dtype), _ptr(x2), x2.stride(0), _ptr(wk),
+            wk.stride(0), int(norm), _rms_eps(), _ptr(kq), _ptr(key), _ptr(inv), _stream_ptr(x2.device))
+    if rc == 2:  # ATTNRES_ERR_UNSUPPORTED
+        return None
+    N.check(rc, "attnres_lrid_fused_key_projection")
+    return kq, key, inv
 
 
 @lrid_fused_projection.register_fake
@@ -1610,9 +1645,11 @@ def lrid_fused_projection_backward(x: Tensor, weight: Tensor, key: Tensor, key_i
         gk = grad_key.to(dt).reshape(n, rank).contiguous()
         if key_norm:
             # the pre-norm key columns, recomputed with the forward's own
-            # [n, rank + query_rank] GEMM (bitwise the values the saved inverse
-            # rms belongs to), so the norm backward works from them in fp32
-            kraw = torch.matmul(x2, w[kq_rows].t())
+            # projection (the tcgen05 kernel, or the [n, rank + query_rank]
+            # library GEMM: bitwise the values the saved inverse rms belongs
+            # to), so the norm backward works from them in fp32
+            tc = _fused_key_projection_tc(x2, w, output_dim, rank, num_heads, key_norm, query_rank, normed=False)
+            kraw = tc[0] if tc is not None else torch.matmul(x2, w[kq_rows].t())
             gkn = torch.empty((n, rank), device=x.device, dtype=dt)
             with torch.cuda.device(x.device):
                 rc = N.load().attnres_head_rms_norm_backward(n, rank, num_heads, _dtype_code(dt), _ptr(gk),

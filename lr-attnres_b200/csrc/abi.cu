@@ -430,6 +430,36 @@ int attnres_lrid_key_projection(int num_sources, int64_t num_tokens, int value_d
   return ATTNRES_OK;
 }
 
+int attnres_lrid_fused_key_projection(int64_t num_tokens, int in_dim, int rank, int query_rank, int num_heads,
+                                      int dtype, const void* x, int64_t x_row_stride, const void* weight,
+                                      int64_t weight_row_stride, int key_norm, float eps, void* key_query,
+                                      void* key, float* key_inv_rms, void* stream) {
+  if (num_tokens < 0 || in_dim < 1 || rank < 1 || query_rank < 0 || num_heads < 1 || rank % num_heads)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT,
+                "attnres_lrid_fused_key_projection: bad geometry (tokens %lld, in_dim %d, rank %d, query_rank %d, "
+                "heads %d)", static_cast<long long>(num_tokens), in_dim, rank, query_rank, num_heads);
+  if (dtype != ATTNRES_DTYPE_F32 && dtype != ATTNRES_DTYPE_F16 && dtype != ATTNRES_DTYPE_BF16)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "attnres_lrid_fused_key_projection: unknown dtype %d", dtype);
+  if (num_tokens == 0) return ATTNRES_OK;
+  if (!x || !weight || !key_query || x_row_stride < in_dim || weight_row_stride < in_dim)
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT,
+                "attnres_lrid_fused_key_projection: NULL pointer or a row stride below in_dim");
+  if (key_norm && (!key || !key_inv_rms))
+    return fail(ATTNRES_ERR_INVALID_ARGUMENT, "attnres_lrid_fused_key_projection: key_norm needs key and key_inv_rms");
+  bool eligible = false;
+  cudaError_t e = attnres::fused_key_projection_launch(num_tokens, in_dim, rank, query_rank, num_heads, dtype, x,
+                                                       x_row_stride, weight, weight_row_stride, key_norm, eps,
+                                                       key_query, key, key_inv_rms,
+                                                       static_cast<cudaStream_t>(stream), &eligible);
+  if (e != cudaSuccess) return cuda_fail(e, "attnres_lrid_fused_key_projection launch");
+  if (!eligible)
+    return fail(ATTNRES_ERR_UNSUPPORTED,
+                "attnres_lrid_fused_key_projection: needs 16-bit data, in_dim %% 64 == 0, rank + query_rank a "
+                "multiple of 16 in [16, 256], a head width that is a multiple of 16 with key_norm, and 16-byte "
+                "aligned rows");
+  return ATTNRES_OK;
+}
+
 int attnres_lrid_key_projection_backward(int num_sources, int64_t num_tokens, int value_dim, int key_dim,
                                          int num_heads, int dtype, const void* const* values,
                                          const int64_t* value_row_strides, void* const* grad_values,

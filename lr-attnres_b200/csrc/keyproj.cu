@@ -39,10 +39,14 @@ struct KeyProjArgs {
   CUtensorMap vmap[kKpMaxSources];  // V_s as [N rows, d cols]
   CUtensorMap wmap;                 // W as [R rows, d cols]
   void* keys;                       // [S][N][R] dtype
-  float* inv_rms;                   // [S][N] or null
+  float* inv_rms;                   // [S][N], or with keys_normed [N][H]; or null
+  // Per-head key norm of the fused output projection (S == 1, no value norm):
+  // the first nrm_cols columns of each row, in H heads, rms-normalised from
+  // their dtype-rounded values into keys_normed [N][nrm_cols]; null = off.
+  void* keys_normed;
   long long N;
   long long ntiles;
-  int S, R, d, tiles_per_src, value_norm;
+  int S, R, d, tiles_per_src, value_norm, H, nrm_cols;
   float eps;
   uint32_t idesc;
 };
@@ -210,10 +214,44 @@ __global__ void __launch_bounds__(192, 1) keyproj_tc_kernel(const __grid_constan
           }
         }
       }
+      if (a.keys_normed != nullptr) {
+        // F.rms_norm per head of the rounded projection (model.py:33-36): the
+        // sum of squares of the head's dtype-rounded values, then each rounded
+        // value times the inverse rms, rounded once more
+        const int dk = a.nrm_cols / a.H;
+        T* np = static_cast<T*>(a.keys_normed) + t * a.nrm_cols;
+        for (int h = 0; h < a.H; ++h) {
+          float hs = 0.f;
+          for (int c0 = h * dk; c0 < (h + 1) * dk; c0 += 16) {
+            float v[16];
+            tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + ab * R + c0, v);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float r = Elem<T>::to_f(Elem<T>::from_f(v[e]));
+              hs = fmaf(r, r, hs);
+            }
+          }
+          const float hinv = rsqrtf(hs / dk + a.eps);
+          for (int c0 = h * dk; c0 < (h + 1) * dk; c0 += 16) {
+            float v[16];
+            tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + ab * R + c0, v);
+            if (t < a.N) {
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                float o[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o[e] = Elem<T>::to_f(Elem<T>::from_f(v[hh * 8 + e])) * hinv;
+                store_pack<T, 8>(np + c0 + hh * 8, o);
+              }
+            }
+          }
+          if (a.inv_rms && t < a.N) a.inv_rms[t * a.H + h] = hinv;
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
-      if (a.inv_rms && t < a.N) a.inv_rms[static_cast<long long>(s) * a.N + t] = inv;
+      if (a.inv_rms && a.keys_normed == nullptr && t < a.N) a.inv_rms[static_cast<long long>(s) * a.N + t] = inv;
     }
   }
   tc_fence_before();
@@ -337,6 +375,64 @@ static bool tc_eligible(int S, long long N, int d, int R, int dtype, const void*
   return al16(w) && (w_stride * 2) % 16 == 0 && encode_fn() != nullptr;
 }
 
+// Fills the shape fields and the instruction descriptor of `a` (sources,
+// tensor maps, outputs and norm fields set by the caller) and launches the
+// tensor-core kernel: one CTA per 128-row tile, up to two CTAs per SM.
+static cudaError_t launch_tc(KeyProjArgs& a, long long N, int d, int R, int dtype, int nsm, cudaStream_t st) {
+  a.N = N;
+  a.R = R;
+  a.d = d;
+  a.tiles_per_src = static_cast<int>((N + kKpRows - 1) / kKpRows);
+  a.ntiles = static_cast<long long>(a.tiles_per_src) * a.S;
+  // kind::f16 instruction descriptor: D f32, A/B bf16 (1) or f16 (0), both K-major, N>>3, M>>4
+  const uint32_t ab = dtype == ATTNRES_DTYPE_BF16 ? 1u : 0u;
+  a.idesc = (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(R >> 3) << 17) |
+            (static_cast<uint32_t>(kKpRows >> 4) << 24);
+  const size_t smem = 1024 + kKpStages * (kKpRows + R) * kKpK * 2 + 256;
+  auto fn = dtype == ATTNRES_DTYPE_BF16 ? keyproj_tc_kernel<__nv_bfloat16> : keyproj_tc_kernel<__half>;
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cached_occupancy(&per_sm, reinterpret_cast<const void*>(fn), 192, smem);
+  if (e != cudaSuccess) return e;
+  per_sm = std::max(1, std::min(per_sm, 2));
+  const long long grid = std::min<long long>(a.ntiles, static_cast<long long>(nsm) * per_sm);
+  fn<<<static_cast<int>(grid), 192, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t fused_key_projection_launch(long long N, int din, int rank, int query_rank, int H, int dtype,
+                                        const void* x, long long x_stride, const void* w, long long w_stride,
+                                        int key_norm, float eps, void* kq, void* key, float* key_inv,
+                                        cudaStream_t st, bool* eligible) {
+  // x [N, din] (row stride x_stride), w the key/query rows [rank + query_rank, din];
+  // kq [N][rank + query_rank] (pre-norm, dtype-rounded), key [N][rank], key_inv [N][H]
+  const int R = rank + query_rank;
+  *eligible = false;
+  if (H < 1 || rank % H) return cudaSuccess;
+  if (key_norm && ((rank / H) % 16 || key == nullptr || key_inv == nullptr)) return cudaSuccess;
+  const int64_t xs = x_stride;
+  if (N < 1 || !tc_eligible(1, N, din, R, dtype, &x, &xs, w, w_stride)) return cudaSuccess;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(kq) || (key_norm && !al16(key))) return cudaSuccess;
+  KeyProjArgs a{};
+  if (!encode_2d(&a.vmap[0], dtype, x, N, din, x_stride, kKpRows) || !encode_2d(&a.wmap, dtype, w, R, din, w_stride, R))
+    return cudaSuccess;
+  int nsm = 0;
+  cudaError_t e = cached_sm_count(&nsm);
+  if (e != cudaSuccess) return e;
+  a.keys = kq;
+  a.S = 1;
+  a.value_norm = 0;
+  a.eps = eps;
+  a.H = H;
+  a.nrm_cols = rank;
+  a.keys_normed = key_norm ? key : nullptr;
+  a.inv_rms = key_norm ? key_inv : nullptr;
+  *eligible = true;
+  return launch_tc(a, N, din, R, dtype, nsm, st);
+}
+
 cudaError_t keyproj_launch(int S, long long N, int d, int R, int dtype, const void* const* values,
                            const int64_t* vstr, const void* w, long long w_stride, int value_norm, float eps,
                            void* keys, float* inv_rms, bool allow_tc, cudaStream_t st, bool* used_tc) {
@@ -354,30 +450,11 @@ cudaError_t keyproj_launch(int S, long long N, int d, int R, int dtype, const vo
     if (ok) {
       a.keys = keys;
       a.inv_rms = inv_rms;
-      a.N = N;
       a.S = S;
-      a.R = R;
-      a.d = d;
-      a.tiles_per_src = static_cast<int>((N + kKpRows - 1) / kKpRows);
-      a.ntiles = static_cast<long long>(a.tiles_per_src) * S;
       a.value_norm = value_norm;
       a.eps = eps;
-      // kind::f16 instruction descriptor: D f32, A/B bf16 (1) or f16 (0), both K-major, N>>3, M>>4
-      const uint32_t ab = dtype == ATTNRES_DTYPE_BF16 ? 1u : 0u;
-      a.idesc = (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(R >> 3) << 17) |
-                (static_cast<uint32_t>(kKpRows >> 4) << 24);
-      const size_t smem = 1024 + kKpStages * (kKpRows + R) * kKpK * 2 + 256;
-      auto fn = dtype == ATTNRES_DTYPE_BF16 ? keyproj_tc_kernel<__nv_bfloat16> : keyproj_tc_kernel<__half>;
-      e = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
-      int per_sm = 0;
-      e = cached_occupancy(&per_sm, reinterpret_cast<const void*>(fn), 192, smem);
-      if (e != cudaSuccess) return e;
-      per_sm = std::max(1, std::min(per_sm, 2));
-      const long long grid = std::min<long long>(a.ntiles, static_cast<long long>(nsm) * per_sm);
-      fn<<<static_cast<int>(grid), 192, smem, st>>>(a);
       *used_tc = true;
-      return cudaGetLastError();
+      return launch_tc(a, N, d, R, dtype, nsm, st);
     }
   }
   KeyProjSimtArgs g{};

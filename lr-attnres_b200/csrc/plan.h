@@ -147,6 +147,13 @@ cudaError_t keyproj_bwd_combine_launch(int S, long long N, int d, int R, int H, 
                                        void* const* grad_values, const void* dn, const void* dk,
                                        const void* keys, const float* inv_rms, const void* g,
                                        const float* alpha, int value_norm, cudaStream_t st);
+// Key/query columns of the fused output projection with the per-head key norm
+// in the tensor-core kernel's epilogue (keyproj.cu); *eligible = false (nothing
+// launched) when the shapes or alignments are outside that kernel.
+cudaError_t fused_key_projection_launch(long long N, int din, int rank, int query_rank, int H, int dtype,
+                                        const void* x, long long x_stride, const void* w, long long w_stride,
+                                        int key_norm, float eps, void* kq, void* key, float* key_inv,
+                                        cudaStream_t st, bool* eligible);
 cudaError_t read_keyproj_status(unsigned* status, bool reset);
 
 // Fused tcgen05 backward of the key projection (keyproj_bwd.cu). Workspace 0

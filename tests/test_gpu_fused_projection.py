@@ -73,3 +73,64 @@ def test_head_rms_norm_reads_a_strided_key_slice():
     xk = kq[:, :R].float().reshape(n, H, R // H)
     want = (xk * torch.rsqrt(xk.pow(2).mean(-1, keepdim=True) + RMS_EPS)).reshape(n, R)
     torch.testing.assert_close(y.float(), want, rtol=2e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,din,R,H,Rq,key_norm", [(300, 384, 64, 2, 32, True), (1000, 1024, 64, 1, 0, True),
+                                                   (129, 256, 32, 2, 0, True), (257, 512, 64, 4, 64, False)])
+def test_fused_key_projection_tensor_core_epilogue(dtype, n, din, R, H, Rq, key_norm):
+    """attnres_lrid_fused_key_projection (tcgen05 GEMM, per-head key norm in
+    the epilogue) through the C ABI: the pre-norm key/query columns against a
+    float64 GEMM of the same rounded inputs, the normalised key and its inverse
+    rms against F.rms_norm per head of the kernel's own rounded columns, and a
+    strided input row (x a column slice of a wider tensor)."""
+    from attnres_b200 import _native as N
+    import ctypes
+
+    torch.manual_seed(n + din + R)
+    code = {torch.bfloat16: 2, torch.float16: 1}[dtype]
+    wide = torch.randn(n, din + 64, device="cuda", dtype=dtype)
+    x = wide[:, 32:32 + din]  # row stride din + 64, 64-byte offset
+    d_out = 128
+    w = (torch.randn(d_out + R + Rq, din, device="cuda") / din ** 0.5).to(dtype)
+    wk = w[d_out:]
+    kq = torch.empty(n, R + Rq, device="cuda", dtype=dtype)
+    key = torch.empty(n, R, device="cuda", dtype=dtype)
+    inv = torch.empty(n, H, device="cuda")
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    rc = N.load().attnres_lrid_fused_key_projection(n, din, R, Rq, H, code, vp(x), x.stride(0), vp(wk), wk.stride(0),
+                                                     int(key_norm), RMS_EPS, vp(kq), vp(key), vp(inv), None)
+    N.check(rc, "attnres_lrid_fused_key_projection")
+    torch.cuda.synchronize()
+    ref = x.double() @ wk.double().t()
+    torch.testing.assert_close(kq.double(), ref, rtol=1e-2, atol=1e-2)
+    if key_norm:
+        kr = kq[:, :R].double().reshape(n, H, R // H)
+        want_inv = torch.rsqrt(kr.pow(2).mean(-1) + RMS_EPS)
+        torch.testing.assert_close(inv.double(), want_inv, rtol=1e-5, atol=1e-6)
+        want = (kr * want_inv.unsqueeze(-1)).reshape(n, R)
+        torch.testing.assert_close(key.double(), want, rtol=1e-2, atol=1e-2)
+
+
+def test_fused_key_projection_rejects_fp32_and_odd_shapes():
+    """fp32 (no tensor-core path at fp32 accuracy) and shapes outside the
+    kernel return ATTNRES_ERR_UNSUPPORTED with nothing launched; the op then
+    takes the library GEMM and the per-head norm kernel."""
+    from attnres_b200 import _native as N
+    import ctypes
+
+    x = torch.randn(64, 384, device="cuda")
+    w = torch.randn(64, 384, device="cuda")
+    out = torch.empty(64, 64, device="cuda")
+    inv = torch.empty(64, 1, device="cuda")
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    L = N.load()
+    assert L.attnres_lrid_fused_key_projection(64, 384, 64, 0, 1, 0, vp(x), 384, vp(w), 384, 1, RMS_EPS, vp(out),
+                                               vp(out), vp(inv), None) == 2
+    xb, wb = x.bfloat16(), w.bfloat16()
+    ob = torch.empty(64, 64, device="cuda", dtype=torch.bfloat16)
+    # in_dim 352 is not a multiple of 64; head width 64 / 8 = 8 is not a multiple of 16
+    assert L.attnres_lrid_fused_key_projection(64, 352, 64, 0, 1, 2, vp(xb), 384, vp(wb), 384, 1, RMS_EPS, vp(ob),
+                                               vp(ob), vp(inv), None) == 2
+    assert L.attnres_lrid_fused_key_projection(64, 384, 64, 0, 8, 2, vp(xb), 384, vp(wb), 384, 1, RMS_EPS, vp(ob),
+                                               vp(ob), vp(inv), None) == 2
