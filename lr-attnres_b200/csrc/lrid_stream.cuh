@@ -127,6 +127,11 @@ __global__ void __launch_bounds__(stream_threads<BWD, SMAX, NORM>(), 1) lrid_str
   float* sm_nrm = sm_dw + HSP;
   T* kcopy = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(sm_logit) + L.off_v);
   T* qcopy = kcopy + S * R;
+  // backward with the output norm: the token's normalised upstream gradient
+  // g' = inv_rms * (g - y * mean<g, y>) per norm group, rounded to T (as the
+  // reference's PyTorch path holds it: the rms-norm backward returns a T
+  // tensor), formed once per token from the g and y rows
+  T* gscr = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(sm_logit) + L.off_g);
   unsigned char* ring = stage0 + static_cast<size_t>(w) * NSW * L.stage_bytes;
   uint64_t* wbars = bars + w * NSW;
   const unsigned long long wait_ns = a.wait_ns;
@@ -219,15 +224,14 @@ __global__ void __launch_bounds__(stream_threads<BWD, SMAX, NORM>(), 1) lrid_str
     } else {
       const int c0 = (c.u - 1 - UY) * CW;
       const uint32_t cb = CW * sizeof(T);
-      if (lane == 0) mbar_arrive_expect_tx(bar, S * cb + (BWD ? (has_y ? 2 : 1) * cb : 0));
+      if (lane == 0) mbar_arrive_expect_tx(bar, S * cb + ((BWD && !has_y) ? cb : 0));
       __syncwarp();
 #pragma unroll
       for (int i = 0; i < NL; ++i) {
         const int s = lane + 32 * i;
         if (go && s < S) bulk_g2s(st + s * cb, vrow[i] + c0, cb, bar);
       }
-      if (BWD && go && lane == (S & 31)) bulk_g2s(st + S * cb, grow + c0, cb, bar);
-      if (BWD && go && has_y && lane == ((S + 1) & 31)) bulk_g2s(st + (S + 1) * cb, yrow + c0, cb, bar);
+      if (BWD && !has_y && go && lane == (S & 31)) bulk_g2s(st + S * cb, grow + c0, cb, bar);
     }
   };
 
@@ -404,7 +408,7 @@ __global__ void __launch_bounds__(stream_threads<BWD, SMAX, NORM>(), 1) lrid_str
       continue;
     }
 
-    if (BWD && u <= UY) {
+    if (has_y && u <= UY) {
       // ---- output-norm backward terms: mean <g, y> per norm group ----------
       const T* gt = reinterpret_cast<const T*>(st);
       const T* yt = gt + d;
@@ -429,6 +433,20 @@ __global__ void __launch_bounds__(stream_threads<BWD, SMAX, NORM>(), 1) lrid_str
           sm_nrm[H + lane] = yi0;
         } else {
           sm_nrm[H + lane] = yinv_next;
+        }
+      }
+      __syncwarp();
+      // g' for the whole row; lane i writes packs i, i + 32, ..., the packs it
+      // reads again in the value chunks
+      for (int h = 0; h < H; ++h) {
+        const float md = sm_nrm[h], yi = sm_nrm[H + h];
+        for (int i = lane; i < ppl; i += 32) {
+          const Pack<T, VEC> gr = lds_pack<T, VEC>(gt + h * dv + i * VEC);
+          const Pack<T, VEC> yr = lds_pack<T, VEC>(yt + h * dv + i * VEC);
+          float o[VEC];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[e] = yi * (Elem<T>::to_f(gr.e[e]) - Elem<T>::to_f(yr.e[e]) * md);
+          store_pack<T, VEC>(gscr + h * dv + i * VEC, o);
         }
       }
       __syncwarp();
@@ -519,16 +537,12 @@ __global__ void __launch_bounds__(stream_threads<BWD, SMAX, NORM>(), 1) lrid_str
       }
     } else {
       float gp[VEC];
-      const Pack<T, VEC> gr = lds_pack<T, VEC>(reinterpret_cast<const T*>(st) + S * CW + lane * VEC);
+      // the upstream-gradient chunk, or with the output norm the token's g'
+      Pack<T, VEC> gr;
+      if constexpr (has_y) gr = lds_pack<T, VEC>(gscr + col);
+      else gr = lds_pack<T, VEC>(reinterpret_cast<const T*>(st) + S * CW + lane * VEC);
 #pragma unroll
       for (int e = 0; e < VEC; ++e) gp[e] = Elem<T>::to_f(gr.e[e]);
-      if (has_y) {
-        // g' = inv_rms * (g - y * mean(g . y)) over the norm group
-        const Pack<T, VEC> yr = lds_pack<T, VEC>(reinterpret_cast<const T*>(st) + (S + 1) * CW + lane * VEC);
-        const float md = sm_nrm[h], yi = sm_nrm[H + h];
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) gp[e] = yi * (gp[e] - Elem<T>::to_f(yr.e[e]) * md);
-      }
 #pragma unroll
       for (int s0 = 0; s0 < SMAX; s0 += 4) {
         if (s0 < S) {
@@ -541,8 +555,7 @@ __global__ void __launch_bounds__(stream_threads<BWD, SMAX, NORM>(), 1) lrid_str
             if (s0 + jj < S) {
               const float wgt = al[s0 + jj];
               if constexpr (kIs16<T>) {
-                if (!has_y) dwp[s0 + jj] = dot_pack16<T, VEC>(dwp[s0 + jj], r4[jj], gr);
-                else dwp[s0 + jj] = dot_pack<T, VEC>(dwp[s0 + jj], gp, r4[jj]);
+                dwp[s0 + jj] = dot_pack16<T, VEC>(dwp[s0 + jj], r4[jj], gr);
               } else {
                 dwp[s0 + jj] = dot_pack<T, VEC>(dwp[s0 + jj], gp, r4[jj]);
               }

@@ -87,11 +87,14 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
   int cap = 0;
   if (cached_smem_optin(&cap) != cudaSuccess) return false;
   const size_t key_unit = static_cast<size_t>(base.S) * base.R * esz + (has_qd ? base.R * esz : 0);
-  const size_t chunk_unit = static_cast<size_t>(base.S) * CW * esz + (bwd ? (has_y ? 2 : 1) * CW * esz : 0);
+  // value chunks carry the g chunk in the backward, except with the output
+  // norm, where g' is formed once per token into the warp's scratch
+  const size_t chunk_unit = static_cast<size_t>(base.S) * CW * esz + ((bwd && !has_y) ? CW * esz : 0);
   const size_t row_unit = (bwd && has_y) ? 2 * static_cast<size_t>(base.d) * esz : 0;
   const size_t sb = align_up(std::max(std::max(key_unit, chunk_unit), row_unit), 128);
   const size_t kcopy_off = align_up(6 * static_cast<size_t>(base.H) * ((base.S + 3) & ~3) * sizeof(float), 16);
-  const size_t wscr = align_up(kcopy_off + (bwd ? key_unit : 0), 128);
+  const size_t gscr_off = align_up(kcopy_off + (bwd ? key_unit : 0), 16);
+  const size_t wscr = align_up(gscr_off + ((bwd && has_y) ? static_cast<size_t>(base.d) * esz : 0), 128);
   const int nsw = std::max(2, std::min(kStreamMaxStages, env_int_w("ATTNRES_STREAM_STAGES", 2)));
   const int nchunks = norm ? (out_norm == ATTNRES_NORM_ROW ? base.d : base.dv) / CW : 0;
   const int max_warps = bwd ? (base.S > 16 ? kStreamBwdWarpsManySources : kStreamBwdWarps)
@@ -113,7 +116,7 @@ bool lrid_warp_plan(const LridPlan& base, int esz, bool bwd, bool has_y, bool ha
       L->off_y = static_cast<int>(wscr_off);
       L->off_qd = static_cast<int>(wscr);
       L->off_v = static_cast<int>(kcopy_off);
-      L->off_g = 0;
+      L->off_g = static_cast<int>(gscr_off);
       L->smem_bytes = static_cast<int>(total);
       L->key_lanes = kl;
       L->key_packs = kp;
