@@ -97,3 +97,38 @@ def test_check_raises_with_library_message():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(N.AttnResError, match="not found"):
         N.load(str(tmp_path / "nope.so"))
+
+
+ERR_INVALID_ARGUMENT = 1  # include/attnres_b200.h
+
+
+@pytest.mark.parametrize("args,msg", [
+    ((64, 384, 64, 0, 0), "bad geometry"),    # no heads
+    ((64, 384, 64, 0, 3), "bad geometry"),    # rank not a multiple of the heads
+    ((-1, 384, 64, 0, 1), "bad geometry"),    # negative token count
+    ((64, 384, 64, -2, 1), "bad geometry"),   # negative query rank
+])
+def test_fused_key_projection_argument_validation(args, msg):
+    """attnres_lrid_fused_key_projection rejects bad geometry with
+    ATTNRES_ERR_INVALID_ARGUMENT and a message, before touching a device."""
+    lib = N.load()
+    n, din, rank, rq, heads = args
+    rc = lib.attnres_lrid_fused_key_projection(n, din, rank, rq, heads, 2, None, din, None, din, 1, 1e-6,
+                                               None, None, None, None)
+    assert rc == ERR_INVALID_ARGUMENT
+    assert msg in lib.attnres_last_error().decode()
+
+
+def test_fused_key_projection_null_pointers_and_zero_tokens():
+    lib = N.load()
+    # zero tokens: nothing to do, no pointer needed
+    assert lib.attnres_lrid_fused_key_projection(0, 384, 64, 0, 1, 2, None, 384, None, 384, 1, 1e-6,
+                                                 None, None, None, None) == 0
+    rc = lib.attnres_lrid_fused_key_projection(64, 384, 64, 0, 1, 2, None, 384, None, 384, 1, 1e-6,
+                                               None, None, None, None)
+    assert rc == ERR_INVALID_ARGUMENT and "NULL" in lib.attnres_last_error().decode()
+    # key_norm needs the normalised-key and inverse-rms outputs
+    fake = ctypes.c_void_p(0x1000)
+    rc = lib.attnres_lrid_fused_key_projection(64, 384, 64, 0, 1, 2, fake, 384, fake, 384, 1, 1e-6,
+                                               fake, None, None, None)
+    assert rc == ERR_INVALID_ARGUMENT and "key_norm" in lib.attnres_last_error().decode()
